@@ -1,0 +1,94 @@
+/*
+ * mms_scan.h -- C ABI of the B200 (sm_100a) selective-scan library
+ * (libmms_scan.so, built from mamba-metal-scan_b200/csrc).
+ *
+ * The scan (reference: Anamaya1729/mamba-metal-scan, mamba_metal/scan.py:13-34):
+ *
+ *     dA[t,d,n] = exp(-dt[t,d] * Aneg[d,n])
+ *     h[t,d,n]  = dA[t,d,n] * h[t-1,d,n] + dt[t,d] * B[t,n] * x[t,d]     h[-1] = 0
+ *     y[t,d]    = sum_n C[t,n] * h[t,d,n]
+ *
+ * Layouts (all float32, C-contiguous, device pointers):
+ *     x, dt, y, dy, dx, ddt   (Bt, T, D)
+ *     Aneg, dAneg             (D, N)
+ *     B, C, dB, dC            (Bt, T, N)
+ *     ckpt                    (Bt, ceil(T/K), D, N): h at the end of every K-step
+ *                             chunk; the last one is h at t = T-1.
+ *
+ * Conventions shared by every entry point:
+ *   - The caller owns all memory. The library never allocates device memory;
+ *     the backward's scratch is a caller-provided workspace whose size comes
+ *     from mms_bwd_workspace_size().
+ *   - Every output is fully written (no accumulation into caller memory, no
+ *     pre-zeroing needed).
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = the legacy default
+ *     stream) and runs asynchronously; nothing synchronises.
+ *   - The return value is an MMS_* status. Argument errors are detected before
+ *     anything is launched. Results are deterministic: no floating-point
+ *     atomics anywhere, fixed reduction order.
+ *   - Supported shapes: N a multiple of 4 with 4 <= N <= 64, K >= 1,
+ *     Bt, D >= 1, T >= 1. B, C, Aneg, ckpt, dB, dC, dAneg must be 16-byte
+ *     aligned (row strides are then 16-byte multiples because N % 4 == 0);
+ *     x, dt, y, dy, dx, ddt need 4-byte alignment.
+ *   - Stateless and reentrant; calls on different streams may overlap.
+ */
+#ifndef MMS_SCAN_H
+#define MMS_SCAN_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MMS_OK 0
+#define MMS_ERR_INVALID_ARG 1      /* a size, stride or pointer is out of range        */
+#define MMS_ERR_UNSUPPORTED_N 2    /* N is not a multiple of 4 in [4, 64]              */
+#define MMS_ERR_WORKSPACE 3        /* workspace NULL or smaller than required           */
+#define MMS_ERR_MISALIGNED 4       /* a pointer violates the alignment rules above      */
+#define MMS_ERR_CUDA 5             /* a kernel launch failed (see cudaGetLastError)      */
+
+/* Version of the ABI in this header (major * 100 + minor). */
+#define MMS_ABI_VERSION 100
+int mms_abi_version(void);
+
+/* Human-readable text for an MMS_* status. Never NULL. */
+const char *mms_status_string(int status);
+
+/*
+ * Forward scan: writes y and ckpt.
+ * Replaces the reference's `lib.ssm_fwd(x, dt, aneg, b_in, c_in, y, ckpt,
+ * bt, t_len, d, chunk, ...)` launch (mamba_metal/scan.py:376-378; kernel
+ * ssm_fwd at scan.py:78-127), including the checkpoint layout (:120-125).
+ */
+int mms_fwd(const float *x, const float *dt, const float *aneg,
+            const float *B, const float *C,
+            float *y, float *ckpt,
+            int Bt, int T, int D, int N, int K, void *stream);
+
+/*
+ * Bytes of device workspace mms_bwd() needs for this shape.
+ * Replaces the reference's process-global (B, K, D, N) scratch buffer
+ * (`_get_scratch`, mamba_metal/scan.py:293-308), which the caller now owns.
+ */
+size_t mms_bwd_workspace_size(int Bt, int T, int D, int N, int K);
+
+/*
+ * Backward scan: from dy and the forward's ckpt, writes dx, ddt, dAneg, dB, dC.
+ * Replaces the reference's `lib.ssm_bwd(x, dt, aneg, b_in, c_in, dy, dx, ddt,
+ * dAneg, dB, dC, ckpt, scratch, bt, t_len, d, chunk, ...)` launch
+ * (mamba_metal/scan.py:406-410; kernel ssm_bwd at scan.py:132-261). Unlike the
+ * reference, dAneg/dB/dC need no zero-fill: they are written, not accumulated.
+ * `workspace` must hold mms_bwd_workspace_size() bytes, 256-byte aligned.
+ */
+int mms_bwd(const float *x, const float *dt, const float *aneg,
+            const float *B, const float *C, const float *dy, const float *ckpt,
+            float *dx, float *ddt, float *daneg, float *dB, float *dC,
+            void *workspace, size_t workspace_bytes,
+            int Bt, int T, int D, int N, int K, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MMS_SCAN_H */

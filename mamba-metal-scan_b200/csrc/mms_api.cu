@@ -1,0 +1,85 @@
+// C ABI of libmms_scan.so (declared in include/mms_scan.h).
+//
+// Argument checking happens here, before anything is launched, so that a bad
+// call returns an MMS_* status instead of reaching a kernel. The checks mirror
+// the reference's host-side validation (mamba_metal/scan.py:274-276 for
+// d_state, :355-365 for shapes) plus what raw pointers add: alignment and
+// NULL checks.
+#include <stdint.h>
+
+#include "mms_kernels.h"
+#include "mms_scan.h"
+
+namespace {
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+int check_shape(int Bt, int T, int D, int N, int K)
+{
+    if (N < 4 || N > 64 || N % 4 != 0) return MMS_ERR_UNSUPPORTED_N;
+    if (Bt < 1 || T < 1 || D < 1 || K < 1) return MMS_ERR_INVALID_ARG;
+    if (Bt > 65535) return MMS_ERR_INVALID_ARG;            // grid.y
+    return MMS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mms_abi_version(void) { return MMS_ABI_VERSION; }
+
+const char *mms_status_string(int status)
+{
+    switch (status) {
+    case MMS_OK: return "ok";
+    case MMS_ERR_INVALID_ARG: return "invalid argument (size out of range or NULL pointer)";
+    case MMS_ERR_UNSUPPORTED_N: return "unsupported d_state: N must be a multiple of 4 in [4, 64]";
+    case MMS_ERR_WORKSPACE: return "workspace missing or smaller than mms_bwd_workspace_size()";
+    case MMS_ERR_MISALIGNED: return "misaligned pointer (B, C, Aneg, ckpt, dB, dC, dAneg need 16 bytes)";
+    case MMS_ERR_CUDA: return "CUDA launch failed";
+    default: return "unknown status";
+    }
+}
+
+int mms_fwd(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
+            float *y, float *ckpt, int Bt, int T, int D, int N, int K, void *stream)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if (!x || !dt || !aneg || !B || !C || !y || !ckpt) return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
+        return MMS_ERR_MISALIGNED;
+    mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K};
+    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
+}
+
+size_t mms_bwd_workspace_size(int Bt, int T, int D, int N, int K)
+{
+    if (check_shape(Bt, T, D, N, K)) return 0;
+    return mms::bwd_workspace_layout(Bt, T, D, N, K).total;
+}
+
+int mms_bwd(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
+            const float *dy, const float *ckpt, float *dx, float *ddt, float *daneg, float *dB,
+            float *dC, void *workspace, size_t workspace_bytes, int Bt, int T, int D, int N, int K,
+            void *stream)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if (!x || !dt || !aneg || !B || !C || !dy || !ckpt || !dx || !ddt || !daneg || !dB || !dC)
+        return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(daneg, 16) || !aligned(dB, 16) || !aligned(dC, 16) || !aligned(x, 4) ||
+        !aligned(dt, 4) || !aligned(dy, 4) || !aligned(dx, 4) || !aligned(ddt, 4))
+        return MMS_ERR_MISALIGNED;
+    const size_t need = mms::bwd_workspace_layout(Bt, T, D, N, K).total;
+    if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
+    mms::BwdArgs a{x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace, Bt, T, D, N, K};
+    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
+}
+
+}  // extern "C"

@@ -1,0 +1,67 @@
+// Shared device helpers for the sm_100a selective-scan kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MMS_LOG2E 1.4426950408889634f
+
+namespace mms {
+
+// 2^x on the MUFU pipe (ex2.approx.ftz.f32). The scan feeds it -dt*Aneg*log2(e),
+// which is <= 0, so the result lies in [0, 1]; flushing denormal results to
+// zero only affects states that have already decayed below 1e-38.
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float4 ld4(const float *p) {
+    return __ldg(reinterpret_cast<const float4 *>(p));
+}
+
+__device__ __forceinline__ void st4(float *p, float4 v) {
+    *reinterpret_cast<float4 *>(p) = v;
+}
+
+__device__ __forceinline__ float comp(const float4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+
+// Transposed butterfly reduction over the lanes selected by lane-bit masks
+// MASK_HI, MASK_HI/2, ..., MASK_LO (powers of two). Each lane starts with NV
+// values v[0..NV); lanes that differ only in those bits hold partials of the
+// same NV sums. At each level a lane keeps half of its values (the upper half
+// if its mask bit is set) and adds the partner's copy of that half, so the
+// work per lane is NV-1 shuffles instead of NV*levels. When a lane is down to
+// one value the remaining levels are plain xor-reductions.
+//
+// On return v[0..nleft) hold complete sums; `first` is the index of v[0] in
+// the original numbering. nleft = max(1, NV >> levels).
+template <int NV, int MASK_HI, int MASK_LO>
+__device__ __forceinline__ void transposed_reduce(float (&v)[NV], int lane, int &first) {
+    first = 0;
+    int cur = NV;
+#pragma unroll
+    for (int m = MASK_HI; m >= MASK_LO && m > 0; m >>= 1) {
+        if (cur > 1) {
+            const int half = cur >> 1;
+            const bool upper = (lane & m) != 0;
+#pragma unroll
+            for (int i = 0; i < NV / 2; ++i) {
+                if (i < half) {
+                    const float send = upper ? v[i] : v[i + half];
+                    const float keep = upper ? v[i + half] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+                }
+            }
+            if (upper) first += half;
+            cur = half;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+        }
+    }
+}
+
+}  // namespace mms

@@ -1,0 +1,47 @@
+// Internal launcher interface between the C ABI (mms_api.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace mms {
+
+struct FwdArgs {
+    const float *x, *dt, *aneg, *B, *C;
+    float *y, *ckpt;
+    int Bt, T, D, N, K;
+};
+
+struct BwdArgs {
+    const float *x, *dt, *aneg, *B, *C, *dy, *ckpt;
+    float *dx, *ddt, *daneg, *dB, *dC;
+    void *workspace;
+    int Bt, T, D, N, K;
+};
+
+// Lanes per channel: ceil(N/4) rounded up to a power of two (N in [4, 64]).
+inline int groups_for(int N)
+{
+    const int q = (N + 3) / 4;
+    int g = 1;
+    while (g < q) g <<= 1;
+    return g;
+}
+
+// Workspace layout of the backward (byte offsets from the workspace base,
+// every region 256-byte aligned).
+struct BwdWorkspace {
+    size_t part_bc;    // (Bt, nblk, T, 2N) per-CTA partial sums of dB|dC over its channels
+    size_t part_a;     // (Bt, D, N) per-batch-row partial sums of dAneg
+    size_t subck;      // (Bt, nseg, D, N) segment-start states inside long chunks
+    size_t total;
+    int nblk;          // CTAs along D
+    int nseg;          // segments per chunk (1 when K <= segment length)
+};
+
+BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K);
+
+cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream);
+cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream);
+
+}  // namespace mms

@@ -1,0 +1,116 @@
+"""ctypes binding of libmms_scan.so (C ABI in include/mms_scan.h).
+
+The library is built in-tree (mamba-metal-scan_b200/build.py) into
+mamba_metal/lib/. There is no fallback: if the library is missing or does not
+load, every CUDA scan call raises RuntimeError naming the problem.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(os.environ.get("MMS_SCAN_LIB", Path(__file__).resolve().parent / "lib" / "libmms_scan.so"))
+
+MMS_OK = 0
+MMS_ERR_INVALID_ARG = 1
+MMS_ERR_UNSUPPORTED_N = 2
+MMS_ERR_WORKSPACE = 3
+MMS_ERR_MISALIGNED = 4
+MMS_ERR_CUDA = 5
+
+# Every symbol include/mms_scan.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+SIGNATURES = {
+    "mms_abi_version": ([], _I),
+    "mms_status_string": ([_I], ctypes.c_char_p),
+    "mms_fwd": ([_P] * 7 + [_I] * 5 + [_P], _I),
+    "mms_bwd_workspace_size": ([_I] * 5, ctypes.c_size_t),
+    "mms_bwd": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raises RuntimeError if unavailable."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                raise RuntimeError(
+                    f"the CUDA selective-scan library is not built: {LIB_PATH} is missing "
+                    "(run `python mamba-metal-scan_b200/build.py`)")
+            try:
+                lib = ctypes.CDLL(str(LIB_PATH))
+            except OSError as e:
+                raise RuntimeError(f"cannot load {LIB_PATH}: {e}") from e
+            for name, (args, res) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.argtypes = args
+                fn.restype = res
+            _lib = lib
+    return _lib
+
+
+def status_string(rc: int) -> str:
+    return load().mms_status_string(rc).decode()
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != MMS_OK:
+        raise RuntimeError(f"{what} failed: status {rc} ({status_string(rc)})")
+
+
+def _ptr(t: torch.Tensor) -> int:
+    return t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def fwd(x, dt, aneg, b_in, c_in, chunk: int):
+    """y (B,T,D) and ckpt (B, ceil(T/chunk), D, N) on the current stream."""
+    lib = load()
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    nchunk = (t_len + chunk - 1) // chunk
+    y = torch.empty(bt, t_len, d, device=x.device, dtype=torch.float32)
+    ckpt = torch.empty(bt, nchunk, d, n, device=x.device, dtype=torch.float32)
+    rc = lib.mms_fwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(y), _ptr(ckpt),
+                     bt, t_len, d, n, chunk, _stream(x.device))
+    _check(rc, "mms_fwd")
+    return y, ckpt
+
+
+def bwd_workspace_size(bt: int, t_len: int, d: int, n: int, chunk: int) -> int:
+    return int(load().mms_bwd_workspace_size(bt, t_len, d, n, chunk))
+
+
+def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None):
+    """(dx, ddt, dAneg, dB, dC) on the current stream."""
+    lib = load()
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    dx = torch.empty_like(x)
+    ddt = torch.empty_like(dt)
+    daneg = torch.empty_like(aneg)
+    db = torch.empty_like(b_in)
+    dc = torch.empty_like(c_in)
+    ws_bytes = bwd_workspace_size(bt, t_len, d, n, chunk)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), device=x.device, dtype=torch.uint8)
+    rc = lib.mms_bwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(dy), _ptr(ckpt),
+                     _ptr(dx), _ptr(ddt), _ptr(daneg), _ptr(db), _ptr(dc),
+                     _ptr(workspace), workspace.numel(),
+                     bt, t_len, d, n, chunk, _stream(x.device))
+    _check(rc, "mms_bwd")
+    return dx, ddt, daneg, db, dc

@@ -1,0 +1,190 @@
+"""Fused selective scan for Mamba on NVIDIA B200 (sm_100a), forward and backward.
+
+Drop-in for the reference package's `mamba_metal.scan`
+(Anamaya1729/mamba-metal-scan, mamba_metal/scan.py): same function names,
+arguments, return values and errors; the Metal kernels are replaced by
+hand-written CUDA kernels in libmms_scan.so, called through its C ABI.
+
+    dA[t,d,n] = exp(-dt[t,d] * Aneg[d,n])
+    h[t,d,n]  = dA[t,d,n] * h[t-1,d,n] + dt[t,d] * B[t,n] * x[t,d]    h[-1] = 0
+    y[t,d]    = sum_n C[t,n] * h[t,d,n]
+
+Shapes: x, dt (B, T, D); Aneg (D, N); B, C (B, T, N); y (B, T, D).
+
+The forward keeps h on chip and writes only a checkpoint of h every `chunk`
+steps; the backward recomputes from those checkpoints and returns gradients
+for all five inputs. Kernels, launch geometry and reductions are described in
+mamba-metal-scan_b200/csrc/. Dispatch (reference scan.py:424-447):
+
+  'cuda'   the CUDA kernels; raises unless every input is a CUDA tensor.
+  'metal'  accepted alias of 'cuda', so configs written for the reference
+           keep working; there is no Metal backend in this build.
+  'torch'  selective_scan_ref, the pure-PyTorch recurrence, on any device.
+  'auto'   the CUDA kernels on CUDA tensors, otherwise None so the caller can
+           fall back to its own path (TinyMamba uses parallel_scan).
+
+On CUDA tensors 'auto', 'cuda' and 'metal' always run the native library; if
+it is missing they raise RuntimeError rather than fall back.
+"""
+from __future__ import annotations
+
+import torch
+
+from mamba_metal import _native
+
+SSM_CHUNK = 64        # K: the forward checkpoints h every K steps
+DBLOCK = 64           # accepted for API compatibility; the CUDA kernels size their own CTAs
+
+_IMPLS = ("auto", "cuda", "metal", "torch")
+
+
+# ------------------------------------------------------- reference (pure torch)
+
+def selective_scan_ref(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                       b_in: torch.Tensor, c_in: torch.Tensor,
+                       return_state: bool = False):
+    """The recurrence left to right in PyTorch ops (reference scan.py:313-333).
+
+    Differentiable through autograd, any device, dtype and d_state. This is
+    the 'torch' implementation; it keeps one (B, D, N) state per step alive
+    for autograd, so it is meant for small shapes and for checking.
+    """
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    h = x.new_zeros(bt, d, n)
+    ys = []
+    for i in range(t_len):
+        dt_i = dt[:, i, :].unsqueeze(-1)
+        h = torch.exp(-dt_i * aneg.unsqueeze(0)) * h \
+            + dt_i * b_in[:, i, :].unsqueeze(1) * x[:, i, :].unsqueeze(-1)
+        ys.append((c_in[:, i, :].unsqueeze(1) * h).sum(-1))
+    y = torch.stack(ys, dim=1) if ys else x.new_zeros(bt, 0, d)
+    return (y, h) if return_state else y
+
+
+# ------------------------------------------------------------------- the kernels
+
+def _aligned(t: torch.Tensor, nbytes: int) -> torch.Tensor:
+    """Contiguous, with a data pointer aligned for the kernels' vector loads."""
+    t = t.contiguous()
+    if t.data_ptr() % nbytes:
+        t = t.clone()
+    return t
+
+
+def _validate(x, dt, aneg, b_in, c_in, impl_name: str):
+    tensors = (x, dt, aneg, b_in, c_in)
+    if not all(t.is_cuda for t in tensors):
+        raise RuntimeError(
+            f"scan_impl={impl_name!r} runs the CUDA kernels and needs every input on a "
+            f"CUDA device (this build has no MPS/Metal backend); saw devices "
+            f"{x.device}, {dt.device}, {aneg.device}, {b_in.device}, {c_in.device}")
+    if len({t.device for t in tensors}) != 1:
+        raise RuntimeError("selective_scan inputs are on different CUDA devices: "
+                           + ", ".join(str(t.device) for t in tensors))
+    if not all(t.dtype == torch.float32 for t in tensors):
+        raise RuntimeError(f"scan_impl={impl_name!r} is fp32-only (the kernels are float32); got "
+                           + ", ".join(str(t.dtype) for t in tensors))
+    if x.dim() != 3 or dt.shape != x.shape or aneg.dim() != 2:
+        raise ValueError(f"bad shapes: x {tuple(x.shape)}, dt {tuple(dt.shape)}, "
+                         f"Aneg {tuple(aneg.shape)}")
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    if aneg.shape[0] != d:
+        raise ValueError(f"Aneg {tuple(aneg.shape)} does not match x's channel count {d}")
+    if b_in.shape != (bt, t_len, n) or c_in.shape != (bt, t_len, n):
+        raise ValueError(f"B {tuple(b_in.shape)} / C {tuple(c_in.shape)} must be "
+                         f"({bt}, {t_len}, {n})")
+    if n % 4 != 0 or n <= 0 or n > 64:
+        raise ValueError(f"d_state must be a positive multiple of 4 no larger than 64 for the "
+                         f"CUDA scan; got {n} (scan_impl='torch' takes any size)")
+
+
+class SelectiveScanCUDA(torch.autograd.Function):
+    """selective_scan_cuda(x, dt, Aneg, B, C) -> y, forward and backward.
+
+    Same contract as the reference's SelectiveScanMetal (scan.py:338-411):
+    inputs are made contiguous, (x, dt, Aneg, B, C, ckpt) are saved, the
+    optional state is the last checkpoint returned detached, and backward
+    returns the five input gradients plus None for chunk, dblock and
+    return_state.
+    """
+
+    @staticmethod
+    def forward(ctx, x, dt, aneg, b_in, c_in, chunk=SSM_CHUNK, dblock=DBLOCK,
+                return_state=False, impl_name="cuda"):
+        _validate(x, dt, aneg, b_in, c_in, impl_name)
+        chunk = int(chunk)
+        if chunk < 1:
+            raise ValueError(f"chunk (the checkpoint stride) must be >= 1; got {chunk}")
+        bt, t_len, d = x.shape
+        n = aneg.shape[1]
+        x = _aligned(x, 4)
+        dt = _aligned(dt, 4)
+        aneg = _aligned(aneg, 16)
+        b_in = _aligned(b_in, 16)
+        c_in = _aligned(c_in, 16)
+        with torch.cuda.device(x.device):
+            if bt == 0 or t_len == 0 or d == 0:
+                y = x.new_zeros(bt, t_len, d)
+                ckpt = x.new_zeros(bt, 0, d, n)
+            else:
+                y, ckpt = _native.fwd(x, dt, aneg, b_in, c_in, chunk)
+        ctx.save_for_backward(x, dt, aneg, b_in, c_in, ckpt)
+        ctx.chunk = chunk
+        if return_state:
+            # The last checkpoint is h at t = T-1; returned detached, as a
+            # snapshot for the recurrent cache (reference scan.py:381-386).
+            state = ckpt[:, -1].detach() if ckpt.shape[1] else x.new_zeros(bt, d, n)
+            return y, state
+        return y
+
+    @staticmethod
+    def backward(ctx, *grads):
+        dy = grads[0]
+        x, dt, aneg, b_in, c_in, ckpt = ctx.saved_tensors
+        bt, t_len, d = x.shape
+        if dy is None or bt == 0 or t_len == 0 or d == 0:
+            return (torch.zeros_like(x), torch.zeros_like(dt), torch.zeros_like(aneg),
+                    torch.zeros_like(b_in), torch.zeros_like(c_in), None, None, None, None)
+        dy = _aligned(dy.float(), 4)
+        with torch.cuda.device(x.device):
+            dx, ddt, daneg, db, dc = _native.bwd(x, dt, aneg, b_in, c_in, dy, ckpt, ctx.chunk)
+        return dx, ddt, daneg, db, dc, None, None, None, None
+
+
+def selective_scan_cuda(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                        b_in: torch.Tensor, c_in: torch.Tensor,
+                        chunk: int = SSM_CHUNK,
+                        dblock: int = DBLOCK,
+                        return_state: bool = False):
+    """y = selective_scan(x, dt, Aneg, B, C) with the CUDA kernels."""
+    return SelectiveScanCUDA.apply(x, dt, aneg, b_in, c_in, chunk, dblock, return_state, "cuda")
+
+
+def selective_scan_metal(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                         b_in: torch.Tensor, c_in: torch.Tensor,
+                         chunk: int = SSM_CHUNK,
+                         dblock: int = DBLOCK,
+                         return_state: bool = False):
+    """The reference's entry point name, kept for drop-in use; runs the CUDA kernels."""
+    return SelectiveScanCUDA.apply(x, dt, aneg, b_in, c_in, chunk, dblock, return_state, "metal")
+
+
+def selective_scan(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                   b_in: torch.Tensor, c_in: torch.Tensor,
+                   impl: str = "auto",
+                   chunk: int = SSM_CHUNK,
+                   return_state: bool = False):
+    """Dispatch the scan on `impl` (see the module docstring)."""
+    if impl == "torch":
+        return selective_scan_ref(x, dt, aneg, b_in, c_in, return_state=return_state)
+    if impl not in _IMPLS:
+        raise ValueError(f"unknown scan_impl {impl!r}; want 'auto', 'cuda', 'metal' or 'torch'")
+    if x.is_cuda:
+        return SelectiveScanCUDA.apply(x, dt, aneg, b_in, c_in, chunk, DBLOCK, return_state,
+                                       "cuda" if impl == "auto" else impl)
+    if impl in ("cuda", "metal"):
+        raise RuntimeError(f"scan_impl={impl!r} needs CUDA tensors (this build has no MPS/Metal "
+                           f"backend); got device {x.device.type!r}")
+    return None
