@@ -4,109 +4,158 @@
 //     dA = exp(-dt*Aneg);  h_t = dA*h_{t-1} + dt*B_t*x_t;  y_t = sum_n C_tn*h_tn
 // with h checkpointed at the end of every K-step chunk and at t = T-1.
 //
-// Work decomposition: one thread owns 4 consecutive states (a "state group")
-// of one (b, d) channel; G = ceil(N/4) rounded up to a power of two lanes
-// share a channel, so a warp covers 32/G channels and a CTA of FWD_WARPS
-// warps covers FWD_WARPS*32/G consecutive channels of one batch row. Compared
-// with one thread per (b, d), this gives G times more threads in flight (the
-// (b,d) count alone cannot fill 148 SMs) and keeps only 4 states, 4 decay
-// rates in registers.
+// Decomposition: a thread owns 4 consecutive states of one (b, d) channel and
+// G = (N/4 rounded up to a power of two) lanes share a channel, so a CTA of
+// FWD_THREADS threads covers DPB = FWD_THREADS/G consecutive channels of one
+// batch row and walks the whole sequence. One thread per (b, d), as in the
+// reference, would leave most of the 148 SMs idle; G lanes per channel give G
+// times the threads and keep only 4 states and 4 decay rates per thread.
 //
-// y_t needs the sum over the G lanes of a channel. Instead of reducing every
-// step, each lane keeps its partial for G consecutive steps and one
-// transposed butterfly (G-1 shuffles) leaves lane g holding the full y for
-// step t0+g, which it stores.
+// Memory: x, dt, B, C arrive in shared memory as time tiles of TT steps,
+// staged by cp.async FWD_STAGES-1 tiles ahead of the compute, so the serial
+// recurrence never waits on DRAM. y_t needs the sum over the channel's G
+// lanes: each lane stores its partial in shared memory and, once per tile,
+// every thread finishes some (t, d) sums and writes y with coalesced stores.
 #include "mms_common.cuh"
 #include "mms_kernels.h"
+#include "mms_stage.cuh"
 
 namespace mms {
 
-constexpr int FWD_WARPS = 4;
+constexpr int FWD_THREADS = 256;
+constexpr int FWD_STAGES = 3;
 
 template <int G>
-__global__ void __launch_bounds__(FWD_WARPS * 32)
+struct FwdShape {
+    static constexpr int DPB = FWD_THREADS / G;            // channels per CTA
+    static constexpr int NPAD = 4 * G;
+    static constexpr int TT = G == 1 ? 8 : 16;             // steps per tile
+    static constexpr int ROWF = 2 * DPB + 2 * NPAD;        // x, dt, B, C floats per step
+    static constexpr size_t SMEM = sizeof(float) * ((size_t)FWD_STAGES * TT * ROWF
+                                                    + (size_t)TT * DPB * G);
+};
+
+template <int G, bool VEC>
+__global__ void __launch_bounds__(FWD_THREADS, 2)
 fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
            const float *__restrict__ Cm, float *__restrict__ y,
            float *__restrict__ ckpt, int T, int D, int N, int K)
 {
-    constexpr int DPW = 32 / G;                      // channels per warp
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
-    const int g = lane & (G - 1);
-    const int d = (blockIdx.x * FWD_WARPS + warp) * DPW + lane / G;
+    using S = FwdShape<G>;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
+    extern __shared__ __align__(16) float smem[];
+    float *tiles = smem;                                   // [STAGES][TT][ROWF]
+    float *ys = smem + FWD_STAGES * TT * ROWF;             // [TT][DPB][G] partial y
+
+    const int tid = threadIdx.x;
+    const int g = tid & (G - 1);
+    const int c = tid / G;                                 // channel within the CTA
+    const int d0 = blockIdx.x * DPB;
+    const int d = d0 + c;
     const int b = blockIdx.y;
-    const bool dval = d < D;
-    const bool act = dval && (4 * g < N);           // masked groups hold zeros
+    const bool act = d < D && 4 * g < N;
     const int nchunk = (T + K - 1) / K;
 
-    // Decay rates pre-scaled by log2(e): dA = 2^(-dt * an).
-    float an[4] = {0.f, 0.f, 0.f, 0.f};
+    float an2[4] = {0.f, 0.f, 0.f, 0.f};                   // Aneg * log2(e)
     if (act) {
         const float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
-        an[0] = a4.x * MMS_LOG2E; an[1] = a4.y * MMS_LOG2E;
-        an[2] = a4.z * MMS_LOG2E; an[3] = a4.w * MMS_LOG2E;
+        an2[0] = a4.x * MMS_LOG2E; an2[1] = a4.y * MMS_LOG2E;
+        an2[2] = a4.z * MMS_LOG2E; an2[3] = a4.w * MMS_LOG2E;
     }
     float h[4] = {0.f, 0.f, 0.f, 0.f};
 
-    const float *xb = x + (size_t)b * T * D + d;
-    const float *dtb = dt + (size_t)b * T * D + d;
-    const float *Bb = Bm + (size_t)b * T * N + 4 * g;
-    const float *Cb = Cm + (size_t)b * T * N + 4 * g;
-    float *yb = y + (size_t)b * T * D + d;
+    const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
+    const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
     float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N + 4 * g;
+    float *yb = y + (size_t)b * T * D;
 
-    int next_ck = min(K, T) - 1;                     // step whose state is checkpointed next
-    int chunk = 0;
-
-    for (int t0 = 0; t0 < T; t0 += G) {
-        float yp[G];
+    const int ntiles = (T + TT - 1) / TT;
 #pragma unroll
-        for (int j = 0; j < G; ++j) {
-            const int t = t0 + j;
-            const bool tv = t < T;
-            float dtv = 0.f, xv = 0.f;
-            float4 Bv = make_float4(0.f, 0.f, 0.f, 0.f), Cv = Bv;
-            if (tv && dval) {
-                dtv = __ldg(dtb + (size_t)t * D);
-                xv = __ldg(xb + (size_t)t * D);
-            }
-            if (tv && act) {
-                Bv = ld4(Bb + (size_t)t * N);
-                Cv = ld4(Cb + (size_t)t * N);
-            }
-            // Padding steps (t >= T) have dt = 0: dA = 1, b = 0, h unchanged.
-            const float ml = -dtv;
-            const float bx = dtv * xv;
+    for (int s = 0; s < FWD_STAGES - 1; ++s) {
+        if (s < ntiles)
+            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
+                                                              s * TT, min(TT, T - s * TT),
+                                                              d0, D, N, tid);
+        cp_commit();
+    }
+
+    int next_ck = min(K, T) - 1;                           // step whose state is checkpointed next
+    int chunk = 0;
+    for (int k = 0; k < ntiles; ++k) {
+        cp_wait<FWD_STAGES - 2>();
+        __syncthreads();
+        const int kn = k + FWD_STAGES - 1;
+        if (kn < ntiles)
+            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(
+                tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, kn * TT, min(TT, T - kn * TT),
+                d0, D, N, tid);
+        cp_commit();
+
+        const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
+        const int t0 = k * TT;
+#pragma unroll
+        for (int j = 0; j < TT; ++j) {
+            const float *row = tile + j * ROWF;
+            // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
+            const float xv = row[c];
+            const float dtv = row[DPB + c];
+            const float4 Bv = *reinterpret_cast<const float4 *>(row + 2 * DPB + 4 * g);
+            const float4 Cv = *reinterpret_cast<const float4 *>(row + 2 * DPB + NPAD + 4 * g);
+            const float ml = -dtv, bx = dtv * xv;
             float acc = 0.f;
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
-                const float a = ex2(ml * an[s]);
+                const float a = ex2(ml * an2[s]);
                 h[s] = fmaf(a, h[s], bx * comp(Bv, s));
                 acc = fmaf(comp(Cv, s), h[s], acc);
             }
-            yp[j] = acc;
-            if (t == next_ck) {                       // uniform across the CTA
+            ys[(j * DPB + c) * G + g] = acc;
+            if (t0 + j == next_ck) {                       // uniform across the CTA
                 if (act) st4(ckb + (size_t)chunk * D * N, make_float4(h[0], h[1], h[2], h[3]));
                 ++chunk;
                 next_ck = min(next_ck + K, T - 1);
             }
         }
-        int first = 0;
-        if constexpr (G > 1) transposed_reduce<G, G / 2, 1>(yp, lane, first);
-        const int t = t0 + first;
-        if (dval && t < T) yb[(size_t)t * D] = yp[0];
+        __syncthreads();
+        // y = sum of the G lane partials; consecutive threads take consecutive channels.
+        for (int p = tid; p < TT * DPB; p += FWD_THREADS) {
+            const int j = p / DPB, cc = p % DPB;
+            const float *src = ys + (size_t)p * G;
+            float sum = 0.f;
+            if constexpr (G >= 4) {
+#pragma unroll
+                for (int q = 0; q < G; q += 4) {
+                    const float4 v = *reinterpret_cast<const float4 *>(src + q);
+                    sum += (v.x + v.y) + (v.z + v.w);
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < G; ++q) sum += src[q];
+            }
+            if (t0 + j < T && d0 + cc < D) yb[(size_t)(t0 + j) * D + d0 + cc] = sum;
+        }
     }
+}
+
+template <int G, bool VEC>
+static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
+{
+    using S = FwdShape<G>;
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<G, VEC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt);
+    fwd_kernel<G, VEC><<<grid, FWD_THREADS, S::SMEM, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
+    return cudaGetLastError();
 }
 
 template <int G>
 static cudaError_t launch_fwd_g(const FwdArgs &a, cudaStream_t stream)
 {
-    constexpr int DPB = FWD_WARPS * 32 / G;          // channels per CTA
-    dim3 grid((a.D + DPB - 1) / DPB, a.Bt);
-    fwd_kernel<G><<<grid, FWD_WARPS * 32, 0, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
-    return cudaGetLastError();
+    return vec_ok(a.D, a.x, a.dt) ? launch_fwd_gv<G, true>(a, stream)
+                                  : launch_fwd_gv<G, false>(a, stream);
 }
 
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)

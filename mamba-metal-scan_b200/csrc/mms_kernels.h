@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdint.h>
 
 namespace mms {
 
@@ -26,6 +27,14 @@ inline int groups_for(int N)
     int g = 1;
     while (g < q) g <<= 1;
     return g;
+}
+
+// 16-byte staging of (T, D) channel arrays is possible when every row starts
+// 16-byte aligned: D % 4 == 0 and 16-byte aligned base pointers.
+inline bool vec_ok(int D, const void *p0, const void *p1, const void *p2 = nullptr)
+{
+    auto al = [](const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return D % 4 == 0 && al(p0) && al(p1) && al(p2);
 }
 
 // Workspace layout of the backward (byte offsets from the workspace base,
