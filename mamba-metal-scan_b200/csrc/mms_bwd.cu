@@ -23,16 +23,27 @@
 //     the group's backward steps: dA_t for dA_t*h_{t-1} and, carried one step,
 //     dA_{t+1} for the adjoint.
 //
-// Memory: every pass reads its time steps from shared-memory tiles of one
-// group (x, dt, dy, B, C for the CTA's channels) staged by cp.async two tiles
-// ahead along the exact order the passes consume them (WorkCursor).
+// Memory: every pass reads GRP-step tiles (x, dt, dy, B, C of the CTA's
+// channels) that cp.async stages in natural layout three groups ahead, along
+// the exact order the passes consume them (WorkCursor). One group ahead of its
+// use, a tile is rewritten in shared memory into the layouts the inner loops
+// read with the fewest instructions: x, dt, dy as per-channel runs of 4 steps
+// (one 16-byte load per 4 steps) and B, C in the lane-specific state orders
+// described next.
+//
+// Arithmetic: the 4 states of a thread are two float2 pairs driven by the
+// packed FFMA2/FMUL2 instructions of sm_100.
 //
 // Reductions, all deterministic (fixed order, no atomics):
 //   * sum over n (dx, ddt): per-lane partials in shared memory, finished once
 //     per group by one thread per (t, d), which also writes dx/ddt coalesced;
-//   * sum over d (dB, dC): transposed butterfly across a warp's channels, the
-//     CTA's warps summed in shared memory once per group and written as one
-//     partial per CTA; reduce_bc_kernel adds the CTAs of a batch row;
+//   * sum over d (dB, dC): a transposed butterfly across a warp's channels.
+//     Each lane holds its 4 states in the order state(r) = r XOR tau, where tau
+//     is made of the lane's two highest channel bits; then at the first two
+//     butterfly levels every lane keeps registers {0,1} and then {0}, so only
+//     the last level (dB vs dC) needs selects. The CTA's warps are summed in
+//     shared memory once per group into one partial per CTA, and
+//     reduce_bc_kernel adds the CTAs of a batch row;
 //   * dAneg: per-thread register sums over the whole walk, one partial per
 //     batch row; reduce_a_kernel adds the rows.
 #include "mms_common.cuh"
@@ -41,31 +52,39 @@
 
 namespace mms {
 
+#ifndef MMS_BWD_GRP
+#define MMS_BWD_GRP 8
+#endif
+#ifndef MMS_BWD_MINB
+#define MMS_BWD_MINB 2
+#endif
+
 constexpr int BWD_THREADS = 256;
 constexpr int BWD_WARPS = BWD_THREADS / 32;
-constexpr int GRP = 8;                    // steps rebuilt per group
-constexpr int SLOTS = 8;                  // groups per segment
-constexpr int SEG = GRP * SLOTS;          // steps per segment
-constexpr int BWD_STAGES = 3;
-
-template <int G>
-constexpr int log2_const() { return G <= 1 ? 0 : 1 + log2_const<G / 2>(); }
+constexpr int GRP = MMS_BWD_GRP;          // steps rebuilt per group
+constexpr int SLOTS = 64 / GRP;           // groups per segment
+constexpr int SEG = GRP * SLOTS;          // steps per segment (64)
+constexpr int NAT_BUFS = 3;               // natural-layout tiles (cp.async targets)
+constexpr int DER_BUFS = 2;               // rewritten tiles (in use, being prepared)
+constexpr float MMS_LN2 = 0.6931471805599453f;
 
 template <int G>
 struct BwdShape {
     static constexpr int DPB = BWD_THREADS / G;            // channels per CTA
-    static constexpr int DPW = 32 / G;                     // channels per warp
     static constexpr int NPAD = 4 * G;
-    static constexpr int ROWF = 3 * DPB + 2 * NPAD;        // x, dt, dy, B, C per step
+    static constexpr int NROWF = 3 * DPB + 2 * NPAD;       // natural row: x, dt, dy, B, C
+    static constexpr int NATF = GRP * NROWF;
+    static constexpr int NPERM = G <= 8 ? 4 : 2;           // distinct tau values
+    static constexpr int QF = GRP * DPB;                   // one array in 4-step runs
+    static constexpr int PF = GRP * NPERM * NPAD;          // B or C in NPERM orders
+    static constexpr int DERF = 3 * QF + 2 * PF;
     static constexpr int NV2 = 2 * NPAD;                   // dB|dC values per step per warp
-    static constexpr int LEV_D = log2_const<DPW>();
-    static constexpr int NLEFT_D = (8 >> LEV_D) > 0 ? (8 >> LEV_D) : 1;
-    static constexpr int DUP_D = G >= 4 ? 0 : (3 & ~(G - 1));   // lanes holding copies
-    static constexpr size_t TILES = (size_t)BWD_STAGES * GRP * ROWF;       // floats
-    static constexpr size_t SLOTF = (size_t)SLOTS * BWD_THREADS * 4;       // floats
-    static constexpr size_t SNF = (size_t)GRP * DPB * G * 2;               // floats
-    static constexpr size_t SDF = (size_t)GRP * BWD_WARPS * NV2;           // floats
-    static constexpr size_t SMEM = sizeof(float) * (TILES + SLOTF + SNF + SDF);
+    static constexpr size_t SLOTF = (size_t)SLOTS * BWD_THREADS * 4;
+    static constexpr size_t SNF = (size_t)GRP * DPB * G * 2;
+    static constexpr size_t SDF = (size_t)GRP * BWD_WARPS * NV2;
+    static constexpr size_t SMEM_K8 =
+        sizeof(float) * ((size_t)NAT_BUFS * NATF + (size_t)DER_BUFS * DERF + SNF + SDF);
+    static constexpr size_t SMEM = SMEM_K8 + sizeof(float) * SLOTF;
 };
 
 // The order in which one CTA consumes GRP-step groups of its batch row:
@@ -115,24 +134,280 @@ struct WorkCursor {
     __device__ int nvalid() const { return phase == 0 ? GRP : min(GRP, u1 - (u0 + j * GRP)); }
 };
 
-// h <- recurrence over the GRP steps of a staged tile (padding steps are zeros).
-template <int DPB, int NPAD, int ROWF>
-__device__ __forceinline__ void advance_tile(float (&h)[4], const float (&an2)[4],
-                                             const float *tile, int c, int g)
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ex2x2(float2 v) { return f2(ex2(v.x), ex2(v.y)); }
+__device__ __forceinline__ float2 lo(float4 v) { return f2(v.x, v.y); }
+__device__ __forceinline__ float2 hi(float4 v) { return f2(v.z, v.w); }
+__device__ __forceinline__ float2 shfl2(float2 v, int m) {
+    return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
+}
+
+// Rewrite a natural tile into the compute layouts (see the file comment).
+template <int G>
+__device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int tid)
 {
-#pragma unroll
-    for (int i = 0; i < GRP; ++i) {
-        const float *row = tile + i * ROWF;
-        const float xv = row[c], dtv = row[DPB + c];
-        const float4 Bv = *reinterpret_cast<const float4 *>(row + 3 * DPB + 4 * g);
-        const float ml = -dtv, bx = dtv * xv;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) h[s] = fmaf(ex2(ml * an2[s]), h[s], bx * comp(Bv, s));
+    using S = BwdShape<G>;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, NROWF = S::NROWF, QF = S::QF, PF = S::PF;
+    constexpr int NQ = GRP / 4;
+    for (int e = tid; e < 3 * NQ * DPB; e += BWD_THREADS) {
+        const int a = e / (NQ * DPB), rem = e % (NQ * DPB);
+        const int q = rem / DPB, cc = rem % DPB;
+        const float *src = nat + (4 * q) * NROWF + a * DPB + cc;
+        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) =
+            make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+    }
+    constexpr int NQ4 = NPAD / 4;
+    for (int e = tid; e < 2 * GRP * S::NPERM * NQ4; e += BWD_THREADS) {
+        const int q4 = e % NQ4;
+        const int pi = (e / NQ4) % S::NPERM;
+        const int i = (e / (NQ4 * S::NPERM)) % GRP;
+        const int a = e / (NQ4 * S::NPERM * GRP);
+        const int tau = S::NPERM == 4 ? pi : 2 * pi;
+        const float *src = nat + i * NROWF + 3 * DPB + a * NPAD + 4 * q4;
+        *reinterpret_cast<float4 *>(der + 3 * QF + a * PF + (i * S::NPERM + pi) * NPAD + 4 * q4) =
+            make_float4(src[0 ^ tau], src[1 ^ tau], src[2 ^ tau], src[3 ^ tau]);
     }
 }
 
+// Per-thread view of a rewritten tile.
+template <int G>
+struct TileView {
+    using S = BwdShape<G>;
+    const float *qx, *qdt, *qdy, *pB, *pC;
+    __device__ TileView(const float *der, int c, int g, int pidx) {
+        qx = der + c * 4;
+        qdt = der + S::QF + c * 4;
+        qdy = der + 2 * S::QF + c * 4;
+        pB = der + 3 * S::QF + pidx * S::NPAD + 4 * g;
+        pC = pB + S::PF;
+    }
+    // 4 consecutive steps [4q, 4q+4) of the thread's channel
+    __device__ float4 x4(int q) const { return *reinterpret_cast<const float4 *>(qx + q * S::DPB * 4); }
+    __device__ float4 dt4(int q) const { return *reinterpret_cast<const float4 *>(qdt + q * S::DPB * 4); }
+    __device__ float4 dy4(int q) const { return *reinterpret_cast<const float4 *>(qdy + q * S::DPB * 4); }
+    // the thread's 4 states of step i in its own state order
+    __device__ float4 B(int i) const { return *reinterpret_cast<const float4 *>(pB + i * S::NPERM * S::NPAD); }
+    __device__ float4 C(int i) const { return *reinterpret_cast<const float4 *>(pC + i * S::NPERM * S::NPAD); }
+};
+
+// h <- recurrence over the GRP steps of a tile (padding steps are zeros).
+template <int G>
+__device__ __forceinline__ void advance_tile(float2 (&h)[2], const float2 (&an2)[2],
+                                             const TileView<G> &v)
+{
+#pragma unroll
+    for (int q = 0; q < GRP / 4; ++q) {
+        const float4 x4 = v.x4(q), d4 = v.dt4(q);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float dtv = comp(d4, k), bx = dtv * comp(x4, k);
+            const float4 Bv = v.B(4 * q + k);
+            const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
+            h[0] = fma2(ex2x2(mul2(md, an2[0])), h[0], mul2(bx2, lo(Bv)));
+            h[1] = fma2(ex2x2(mul2(md, an2[1])), h[1], mul2(bx2, hi(Bv)));
+        }
+    }
+}
+
+// Per-thread constants shared by both backward kernels.
+template <int G>
+struct Lane {
+    using S = BwdShape<G>;
+    int tid, lane, warp, g, c, d0, d, b, tau, pidx, u3, sd_pos;
+    bool act, sd_writer;
+    float2 an2[2];                                  // Aneg * log2(e) in lane state order
+
+    __device__ Lane(const float *aneg, int D, int N) {
+        tid = threadIdx.x;
+        lane = tid & 31;
+        warp = tid >> 5;
+        g = tid & (G - 1);
+        c = tid / G;
+        d0 = blockIdx.x * S::DPB;
+        d = d0 + c;
+        b = blockIdx.y;
+        act = d < D && (4 * g < N);
+        // Lane-specific state order: register r holds state 4g + (r ^ tau).
+        const int u1 = (lane >> 4) & 1;
+        const int u2 = G <= 8 ? (lane >> 3) & 1 : 0;
+        tau = 2 * u1 + u2;
+        pidx = S::NPERM == 4 ? tau : u1;
+        u3 = G <= 4 ? (lane >> 2) & 1 : 0;          // dB (0) / dC (1) kept at the last level
+        // Output position of this lane's dB/dC value after the butterfly
+        // (G <= 4: kind u3, state tau; G >= 8 writes several values).
+        sd_pos = (G <= 4 ? u3 * S::NPAD : 0) + 4 * g + tau;
+        sd_writer = G >= 4 || (lane & (G == 2 ? 2 : 3)) == 0;
+        an2[0] = f2(0.f, 0.f);
+        an2[1] = f2(0.f, 0.f);
+        if (act) {
+            const float *ap = aneg + (size_t)d * N + 4 * g;
+            an2[0] = f2(__ldg(ap + (0 ^ tau)) * MMS_LOG2E, __ldg(ap + (1 ^ tau)) * MMS_LOG2E);
+            an2[1] = f2(__ldg(ap + (2 ^ tau)) * MMS_LOG2E, __ldg(ap + (3 ^ tau)) * MMS_LOG2E);
+        }
+    }
+    // The 4 states of channel d, group g, in lane order, from a (D, N) plane.
+    __device__ void load_state(float2 (&h)[2], const float *plane_base, int N) const {
+        float hh[4] = {0.f, 0.f, 0.f, 0.f};
+        if (act) {
+            const float *p = plane_base + (size_t)d * N + 4 * g;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) hh[r] = __ldg(p + (r ^ tau));
+        }
+        h[0] = f2(hh[0], hh[1]);
+        h[1] = f2(hh[2], hh[3]);
+    }
+};
+
+// Carried across the backward walk.
+struct Adjoint {
+    float2 gad[2];      // adjoint g of the most recent (later) step
+    float2 anx[2];      // dA of the step after it; zero past the end of the sequence
+    float2 dac[2];      // sum_t dt*g*dA*h_{t-1}
+};
+
+// Rebuild one group from the state entering it, then walk it backwards,
+// leaving the group's dx/ddt partials in sn and per-warp dB/dC sums in sd.
+template <int G, bool FULL>
+__device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&hb)[2],
+                                           const Lane<G> &L, Adjoint &A, int nv,
+                                           float *sn, float *sd)
+{
+    using S = BwdShape<G>;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, NV2 = S::NV2;
+    float2 av[GRP][2], hv[GRP][2];
+#pragma unroll
+    for (int q = 0; q < GRP / 4; ++q) {
+        const float4 x4 = v.x4(q), d4 = v.dt4(q);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = 4 * q + k;
+            const float dtv = comp(d4, k), bx = dtv * comp(x4, k);
+            const float4 Bv = v.B(i);
+            const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
+            av[i][0] = ex2x2(mul2(md, L.an2[0]));
+            av[i][1] = ex2x2(mul2(md, L.an2[1]));
+            hv[i][0] = fma2(av[i][0], i ? hv[i > 0 ? i - 1 : 0][0] : hb[0], mul2(bx2, lo(Bv)));
+            hv[i][1] = fma2(av[i][1], i ? hv[i > 0 ? i - 1 : 0][1] : hb[1], mul2(bx2, hi(Bv)));
+        }
+    }
+#pragma unroll
+    for (int q = GRP / 4 - 1; q >= 0; --q) {
+        const float4 x4 = v.x4(q), d4 = v.dt4(q), y4 = v.dy4(q);
+#pragma unroll
+        for (int k = 3; k >= 0; --k) {
+            const int i = 4 * q + k;
+            if (!FULL && i >= nv) continue;           // uniform
+            const float dtv = comp(d4, k), xv = comp(x4, k), dyv = comp(y4, k);
+            const float4 Bv = v.B(i), Cv = v.C(i);
+            const float2 dy2 = f2(dyv, dyv), dt2 = f2(dtv, dtv);
+            const float dxv = dtv * xv;
+            const float2 dxv2 = f2(dxv, dxv);
+            float2 p1 = f2(0.f, 0.f), p2 = f2(0.f, 0.f), vb[2], vc[2];
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+                float2 a1 = A.anx[p];
+                if (i + 1 < GRP) {
+                    const float2 an = av[i + 1 < GRP ? i + 1 : i][p];
+                    if (FULL) a1 = an;
+                    else if (i + 1 < nv) a1 = an;
+                }
+                const float2 cp = p ? hi(Cv) : lo(Cv);
+                const float2 bp = p ? hi(Bv) : lo(Bv);
+                A.gad[p] = fma2(a1, A.gad[p], mul2(dy2, cp));
+                const float2 hp = i ? hv[i > 0 ? i - 1 : 0][p] : hb[p];
+                const float2 u = mul2(A.gad[p], mul2(av[i][p], hp));
+                p1 = fma2(A.gad[p], bp, p1);
+                p2 = fma2(L.an2[p], u, p2);
+                A.dac[p] = fma2(dt2, u, A.dac[p]);
+                vb[p] = mul2(A.gad[p], dxv2);
+                vc[p] = mul2(dy2, hv[i][p]);
+            }
+            *reinterpret_cast<float2 *>(sn + ((i * DPB + L.c) * G + L.g) * 2) =
+                f2(p1.x + p1.y, p2.x + p2.y);
+            // dB|dC butterfly across the warp's channels
+            vb[0] = add2(vb[0], shfl2(vb[1], 16));
+            vc[0] = add2(vc[0], shfl2(vc[1], 16));
+            float *r = sd + (i * BWD_WARPS + L.warp) * NV2;
+            if constexpr (G == 16) {
+                r[4 * L.g + L.tau] = vb[0].x;
+                r[4 * L.g + (L.tau ^ 1)] = vb[0].y;
+                r[NPAD + 4 * L.g + L.tau] = vc[0].x;
+                r[NPAD + 4 * L.g + (L.tau ^ 1)] = vc[0].y;
+            } else {
+                const float2 s2 = add2(f2(vb[0].x, vc[0].x),
+                                       f2(__shfl_xor_sync(0xffffffffu, vb[0].y, 8),
+                                          __shfl_xor_sync(0xffffffffu, vc[0].y, 8)));
+                if constexpr (G == 8) {
+                    r[4 * L.g + L.tau] = s2.x;
+                    r[NPAD + 4 * L.g + L.tau] = s2.y;
+                } else {
+                    const float send = L.u3 ? s2.x : s2.y;
+                    float keep = L.u3 ? s2.y : s2.x;
+                    keep += __shfl_xor_sync(0xffffffffu, send, 4);
+                    if constexpr (G <= 2) keep += __shfl_xor_sync(0xffffffffu, keep, 2);
+                    if constexpr (G == 1) keep += __shfl_xor_sync(0xffffffffu, keep, 1);
+                    if (L.sd_writer) r[L.sd_pos] = keep;
+                }
+            }
+        }
+    }
+    A.anx[0] = av[0][0];
+    A.anx[1] = av[0][1];
+}
+
+// After a barrier: finish the group's sums. dx, ddt: one thread per (t, d),
+// coalesced stores. dB, dC: sum of the CTA's warps, this CTA's partial.
+template <int G>
+__device__ __forceinline__ void flush_group(const float *dtile, const float *sn, const float *sd,
+                                            int tid, int t0, int nv, int d0, int D, int N,
+                                            float *dxb, float *ddtb, float *pbc)
+{
+    using S = BwdShape<G>;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, NV2 = S::NV2;
+    for (int p = tid; p < GRP * DPB; p += BWD_THREADS) {
+        const int i = p / DPB, cc = p % DPB;
+        if (i >= nv) break;
+        const float *src = sn + (size_t)p * G * 2;
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int q = 0; q < G; ++q) { s1 += src[2 * q]; s2 += src[2 * q + 1]; }
+        const int o = ((i >> 2) * DPB + cc) * 4 + (i & 3);
+        if (d0 + cc < D) {
+            const size_t go = (size_t)(t0 + i) * D + d0 + cc;
+            dxb[go] = dtile[S::QF + o] * s1;
+            ddtb[go] = fmaf(dtile[o], s1, -s2 * MMS_LN2);
+        }
+    }
+    for (int p = tid; p < GRP * NV2; p += BWD_THREADS) {
+        const int i = p / NV2, jj = p % NV2;
+        if (i >= nv) break;
+        const int kind = jj / NPAD, n = jj % NPAD;
+        const float *rr = sd + i * BWD_WARPS * NV2 + jj;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < BWD_WARPS; ++w) sum += rr[w * NV2];
+        if (n < N) pbc[(size_t)(t0 + i) * 2 * N + kind * N + n] = sum;
+    }
+}
+
+template <int G>
+__device__ __forceinline__ void store_dacc(const Lane<G> &L, const Adjoint &A, float *part_a,
+                                           int D, int N)
+{
+    if (!L.act) return;
+    float *pa = part_a + ((size_t)L.b * D + L.d) * N + 4 * L.g;
+    pa[0 ^ L.tau] = -A.dac[0].x;
+    pa[1 ^ L.tau] = -A.dac[0].y;
+    pa[2 ^ L.tau] = -A.dac[1].x;
+    pa[3 ^ L.tau] = -A.dac[1].y;
+}
+
+// General backward: any checkpoint stride K (see the file comment).
 template <int G, bool VEC>
-__global__ void __launch_bounds__(BWD_THREADS, 2)
+__global__ void __launch_bounds__(BWD_THREADS, MMS_BWD_MINB)
 bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
            const float *__restrict__ Cm, const float *__restrict__ dy,
@@ -142,204 +417,204 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            int T, int D, int N, int K, int nblk, int nsegk)
 {
     using S = BwdShape<G>;
-    constexpr int DPB = S::DPB, NPAD = S::NPAD, ROWF = S::ROWF, NV2 = S::NV2;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD;
     extern __shared__ __align__(16) float smem[];
-    float *tiles = smem;                                             // [STAGES][GRP][ROWF]
-    float4 *slots = reinterpret_cast<float4 *>(smem + S::TILES);    // [SLOTS][THREADS]
-    float *sn = smem + S::TILES + S::SLOTF;                          // [GRP][DPB][G][2]
+    float *nat = smem;                                               // [NAT_BUFS][NATF]
+    float *der = nat + NAT_BUFS * S::NATF;                           // [DER_BUFS][DERF]
+    float *sn = der + DER_BUFS * S::DERF;                            // [GRP][DPB][G][2]
     float *sd = sn + S::SNF;                                         // [GRP][WARPS][NV2]
+    float4 *slots = reinterpret_cast<float4 *>(sd + S::SDF);         // [SLOTS][THREADS]
 
-    const int tid = threadIdx.x;
-    const int lane = tid & 31, warp = tid >> 5;
-    const int g = tid & (G - 1);
-    const int c = tid / G;
-    const int d0 = blockIdx.x * DPB;
-    const int d = d0 + c;
-    const int b = blockIdx.y;
-    const bool act = d < D && (4 * g < N);
+    const Lane<G> L(aneg, D, N);
+    const int tid = L.tid;
     const int nchunk = (T + K - 1) / K;
-    const int twoN = 2 * N;
-
-    float an[4] = {0.f, 0.f, 0.f, 0.f}, an2[4];
-    if (act) {
-        const float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
-        an[0] = a4.x; an[1] = a4.y; an[2] = a4.z; an[3] = a4.w;
-    }
-#pragma unroll
-    for (int s = 0; s < 4; ++s) an2[s] = an[s] * MMS_LOG2E;
-
     const size_t plane = (size_t)D * N;
-    const size_t chan = (size_t)d * N + 4 * g;
-    const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
-    const float *dyb = dy + (size_t)b * T * D;
-    const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
-    float *dxb = dx + (size_t)b * T * D;
-    float *ddtb = ddt + (size_t)b * T * D;
-    float *pbc = part_bc + ((size_t)b * nblk + blockIdx.x) * T * twoN;
+    const size_t chan = (size_t)L.d * N + 4 * L.g;
+    const size_t rowD = (size_t)L.b * T * D;
+    const float *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
+    const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
+    float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
 
     WorkCursor cur, pre;
     cur.start(T, K);
     pre = cur;
 #pragma unroll
-    for (int s = 0; s < BWD_STAGES - 1; ++s) {
+    for (int s = 0; s < NAT_BUFS; ++s) {
         if (!pre.done()) {
             stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
-                tiles + s * GRP * ROWF, xb, dtb, dyb, Bb, Cb, pre.tstart(), pre.nvalid(), d0, D, N, tid);
+                nat + s * S::NATF, xb, dtb, dyb, Bb, Cb, pre.tstart(), pre.nvalid(), L.d0, D, N, tid);
             pre.advance();
         }
         cp_commit();
     }
+    cp_wait<NAT_BUFS - 1>();
+    __syncthreads();
+    rewrite_tile<G>(nat, der, tid);
 
-    float gad[4] = {0.f, 0.f, 0.f, 0.f};    // adjoint g, carried across steps
-    float anx[4] = {0.f, 0.f, 0.f, 0.f};    // dA_{t+1}; zero past the end
-    float dac[4] = {0.f, 0.f, 0.f, 0.f};    // sum_t dt*g*dA*h_{t-1}
-    float hc[4], hq[4], hs[4];
+    Adjoint A;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+    float2 hs[2];
     int cur_chunk = -1, cur_seg = -1;
 
     for (int it = 0; !cur.done(); ++it, cur.advance()) {
-        cp_wait<BWD_STAGES - 2>();
-        __syncthreads();
-        if (!pre.done()) {
+        cp_wait<NAT_BUFS - 2>();                      // this thread's copies of item it+1
+        __syncthreads();                              // everyone's copies; item it rewritten
+        {
+            WorkCursor nxt = cur;
+            nxt.advance();
+            if (!nxt.done())
+                rewrite_tile<G>(nat + ((it + 1) % NAT_BUFS) * S::NATF,
+                                der + ((it + 1) % DER_BUFS) * S::DERF, tid);
+        }
+        if (!pre.done()) {                            // item it+3 into item it's natural tile
             stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
-                tiles + ((it + BWD_STAGES - 1) % BWD_STAGES) * GRP * ROWF, xb, dtb, dyb, Bb, Cb,
-                pre.tstart(), pre.nvalid(), d0, D, N, tid);
+                nat + ((it + NAT_BUFS) % NAT_BUFS) * S::NATF, xb, dtb, dyb, Bb, Cb,
+                pre.tstart(), pre.nvalid(), L.d0, D, N, tid);
             pre.advance();
         }
         cp_commit();
-        const float *tile = tiles + (it % BWD_STAGES) * GRP * ROWF;
+        const float *dtile = der + (it % DER_BUFS) * S::DERF;
+        const TileView<G> v(dtile, L.c, L.g, L.pidx);
 
-        if (cur.c != cur_chunk) {                      // first group of a chunk
+        if (cur.c != cur_chunk) {                     // first group of a chunk
             cur_chunk = cur.c;
             cur_seg = -1;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (cur.c > 0 && act) v = ld4(ckpt + ((size_t)b * nchunk + (cur.c - 1)) * plane + chan);
-            hc[0] = v.x; hc[1] = v.y; hc[2] = v.z; hc[3] = v.w;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) hq[s] = hc[s];
+            if (cur.phase == 0) {
+                if (cur.c > 0) L.load_state(hs, ckpt + ((size_t)L.b * nchunk + cur.c - 1) * plane, N);
+                else hs[0] = hs[1] = f2(0.f, 0.f);
+            }
         }
-        if (cur.phase == 0) {                          // pre-pass: segment-start states
-            advance_tile<DPB, NPAD, ROWF>(hq, an2, tile, c, g);
-            if ((cur.j + 1) % SLOTS == 0 && act) {
+        if (cur.phase == 0) {                         // pre-pass: segment-start states
+            advance_tile<G>(hs, L.an2, v);
+            if ((cur.j + 1) % SLOTS == 0 && L.act) {
                 const int q = (cur.j + 1) / SLOTS;
-                *reinterpret_cast<float4 *>(subck + ((size_t)b * nsegk + q) * plane + chan) =
-                    make_float4(hq[0], hq[1], hq[2], hq[3]);
+                *reinterpret_cast<float4 *>(subck + ((size_t)L.b * nsegk + q) * plane + chan) =
+                    make_float4(hs[0].x, hs[0].y, hs[1].x, hs[1].y);
             }
             continue;
         }
-        if (cur.sg != cur_seg) {                       // first group of a segment
+        if (cur.sg != cur_seg) {                      // first group of a segment
             cur_seg = cur.sg;
-            if (cur.sg == 0) {
-#pragma unroll
-                for (int s = 0; s < 4; ++s) hs[s] = hc[s];
-            } else {
+            if (cur.sg > 0) {
                 // written by this same thread in the pre-pass: coherent plain load
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (act) v = *reinterpret_cast<const float4 *>(
-                    subck + ((size_t)b * nsegk + cur.sg) * plane + chan);
-                hs[0] = v.x; hs[1] = v.y; hs[2] = v.z; hs[3] = v.w;
+                float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (L.act) w = *reinterpret_cast<const float4 *>(
+                    subck + ((size_t)L.b * nsegk + cur.sg) * plane + chan);
+                hs[0] = lo(w);
+                hs[1] = hi(w);
+            } else if (cur.c > 0) {
+                L.load_state(hs, ckpt + ((size_t)L.b * nchunk + cur.c - 1) * plane, N);
+            } else {
+                hs[0] = hs[1] = f2(0.f, 0.f);
             }
         }
-        if (cur.phase == 1) {                          // recompute: keep group-entry states
-            slots[cur.j * BWD_THREADS + tid] = make_float4(hs[0], hs[1], hs[2], hs[3]);
-            advance_tile<DPB, NPAD, ROWF>(hs, an2, tile, c, g);
+        if (cur.phase == 1) {                         // recompute: keep group-entry states
+            slots[cur.j * BWD_THREADS + tid] = make_float4(hs[0].x, hs[0].y, hs[1].x, hs[1].y);
+            advance_tile<G>(hs, L.an2, v);
             continue;
         }
 
         // ---- walk one group backwards
-        const int j = cur.j;
         const int nv = cur.nvalid();
         const int t0 = cur.tstart();
-        float hb[4];
-        if (j == cur.ngrp - 1) {
-#pragma unroll
-            for (int s = 0; s < 4; ++s) hb[s] = hs[s];
+        float2 hb[2];
+        if (cur.j == cur.ngrp - 1) {
+            hb[0] = hs[0];
+            hb[1] = hs[1];
         } else {
-            const float4 v = slots[j * BWD_THREADS + tid];
-            hb[0] = v.x; hb[1] = v.y; hb[2] = v.z; hb[3] = v.w;
+            const float4 w = slots[cur.j * BWD_THREADS + tid];
+            hb[0] = lo(w);
+            hb[1] = hi(w);
         }
-        float av[GRP][4], hv[GRP][4];
-#pragma unroll
-        for (int i = 0; i < GRP; ++i) {
-            const float *row = tile + i * ROWF;
-            const float xv = row[c], dtv = row[DPB + c];
-            const float4 Bv = *reinterpret_cast<const float4 *>(row + 3 * DPB + 4 * g);
-            const float ml = -dtv, bx = dtv * xv;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                av[i][s] = ex2(ml * an2[s]);
-                hv[i][s] = fmaf(av[i][s], i ? hv[i > 0 ? i - 1 : 0][s] : hb[s], bx * comp(Bv, s));
-            }
-        }
-#pragma unroll
-        for (int i = GRP - 1; i >= 0; --i) {
-            if (i < nv) {                               // uniform
-                const float *row = tile + i * ROWF;
-                const float xv = row[c], dtv = row[DPB + c], dyv = row[2 * DPB + c];
-                const float4 Bv = *reinterpret_cast<const float4 *>(row + 3 * DPB + 4 * g);
-                const float4 Cv = *reinterpret_cast<const float4 *>(row + 3 * DPB + NPAD + 4 * g);
-                const float dxv = dtv * xv;
-                float p1 = 0.f, p2 = 0.f, vbc[8];
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
-                    float a1 = anx[s];
-                    if (i + 1 < GRP) {
-                        if (i + 1 < nv) a1 = av[i + 1 < GRP ? i + 1 : i][s];
-                    }
-                    gad[s] = fmaf(a1, gad[s], dyv * comp(Cv, s));
-                    const float hp = i ? hv[i > 0 ? i - 1 : 0][s] : hb[s];
-                    const float u = gad[s] * (av[i][s] * hp);
-                    p1 = fmaf(gad[s], comp(Bv, s), p1);
-                    p2 = fmaf(an[s], u, p2);
-                    dac[s] = fmaf(dtv, u, dac[s]);
-                    vbc[s] = gad[s] * dxv;
-                    vbc[4 + s] = dyv * hv[i][s];
-                }
-                *reinterpret_cast<float2 *>(sn + ((i * DPB + c) * G + g) * 2) = make_float2(p1, p2);
-                int fb;
-                transposed_reduce<8, 16, G>(vbc, lane, fb);
-                if ((lane & S::DUP_D) == 0) {
-                    float *r = sd + (i * BWD_WARPS + warp) * NV2;
-#pragma unroll
-                    for (int k2 = 0; k2 < S::NLEFT_D; ++k2) {
-                        const int idx = fb + k2;
-                        r[idx < 4 ? 4 * g + idx : NPAD + 4 * g + idx - 4] = vbc[k2];
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int s = 0; s < 4; ++s) anx[s] = av[0][s];
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, sn, sd);
+        else walk_group<G, false>(v, hb, L, A, nv, sn, sd);
         __syncthreads();
-        // dx, ddt: finish the sums over n, one thread per (t, d), coalesced stores
-        for (int p = tid; p < nv * DPB; p += BWD_THREADS) {
-            const int i = p / DPB, cc = p % DPB;
-            const float *src = sn + (size_t)p * G * 2;
-            float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-            for (int q = 0; q < G; ++q) { s1 += src[2 * q]; s2 += src[2 * q + 1]; }
-            const float *row = tile + i * ROWF;
-            if (d0 + cc < D) {
-                const size_t o = (size_t)(t0 + i) * D + d0 + cc;
-                dxb[o] = row[DPB + cc] * s1;
-                ddtb[o] = fmaf(row[cc], s1, -s2);
-            }
-        }
-        // dB, dC: this CTA's partial for the group's steps
-        for (int p = tid; p < nv * twoN; p += BWD_THREADS) {
-            const int i = p / twoN, jj = p - i * twoN;
-            const int pos = jj < N ? jj : NPAD + jj - N;
-            const float *r = sd + i * BWD_WARPS * NV2 + pos;
-            float sum = 0.f;
-#pragma unroll
-            for (int w = 0; w < BWD_WARPS; ++w) sum += r[w * NV2];
-            pbc[(size_t)(t0 + i) * twoN + jj] = sum;
-        }
+        flush_group<G>(dtile, sn, sd, tid, t0, nv, L.d0, D, N, dx + rowD, ddt + rowD, pbc);
     }
     cp_wait<0>();
-    if (act) {
-        float *pa = part_a + (size_t)b * plane + chan;
-        st4(pa, make_float4(-dac[0], -dac[1], -dac[2], -dac[3]));
+    store_dacc<G>(L, A, part_a, D, N);
+}
+
+// Backward for checkpoint stride K == GRP: every chunk is one group whose
+// entry state is the forward's checkpoint, so there is no recompute pass and
+// no slot storage; groups are simply chunks nchunk-1 .. 0.
+template <int G, bool VEC>
+__global__ void __launch_bounds__(BWD_THREADS, 2)
+bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
+              const float *__restrict__ aneg, const float *__restrict__ Bm,
+              const float *__restrict__ Cm, const float *__restrict__ dy,
+              const float *__restrict__ ckpt, float *__restrict__ dx,
+              float *__restrict__ ddt, float *__restrict__ part_bc,
+              float *__restrict__ part_a, int T, int D, int N, int nblk)
+{
+    using S = BwdShape<G>;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD;
+    extern __shared__ __align__(16) float smem[];
+    float *nat = smem;
+    float *der = nat + NAT_BUFS * S::NATF;
+    float *sn = der + DER_BUFS * S::DERF;
+    float *sd = sn + S::SNF;
+
+    const Lane<G> L(aneg, D, N);
+    const int tid = L.tid;
+    const int nchunk = (T + GRP - 1) / GRP;
+    const size_t plane = (size_t)D * N;
+    const size_t rowD = (size_t)L.b * T * D;
+    const float *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
+    const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
+    const float *ckb = ckpt + (size_t)L.b * nchunk * plane;
+    float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
+
+#pragma unroll
+    for (int s = 0; s < NAT_BUFS; ++s) {
+        const int c = nchunk - 1 - s;
+        if (c >= 0)
+            stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
+                nat + s * S::NATF, xb, dtb, dyb, Bb, Cb, c * GRP, min(GRP, T - c * GRP),
+                L.d0, D, N, tid);
+        cp_commit();
     }
+    float2 hnext[2];                                   // state entering the next group
+    if (nchunk >= 2) L.load_state(hnext, ckb + (size_t)(nchunk - 2) * plane, N);
+    else hnext[0] = hnext[1] = f2(0.f, 0.f);
+    cp_wait<NAT_BUFS - 1>();
+    __syncthreads();
+    rewrite_tile<G>(nat, der, tid);
+
+    Adjoint A;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+
+    for (int it = 0; it < nchunk; ++it) {
+        const int c = nchunk - 1 - it;
+        cp_wait<NAT_BUFS - 2>();
+        __syncthreads();
+        if (c >= 1)
+            rewrite_tile<G>(nat + ((it + 1) % NAT_BUFS) * S::NATF,
+                            der + ((it + 1) % DER_BUFS) * S::DERF, tid);
+        if (c >= NAT_BUFS) {
+            const int cs = c - NAT_BUFS;
+            stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
+                nat + ((it + NAT_BUFS) % NAT_BUFS) * S::NATF, xb, dtb, dyb, Bb, Cb, cs * GRP,
+                GRP, L.d0, D, N, tid);
+        }
+        cp_commit();
+        const float2 hb[2] = {hnext[0], hnext[1]};
+        if (c >= 2) L.load_state(hnext, ckb + (size_t)(c - 2) * plane, N);
+        else hnext[0] = hnext[1] = f2(0.f, 0.f);
+
+        const float *dtile = der + (it % DER_BUFS) * S::DERF;
+        const TileView<G> v(dtile, L.c, L.g, L.pidx);
+        const int t0 = c * GRP;
+        const int nv = min(GRP, T - t0);
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, sn, sd);
+        else walk_group<G, false>(v, hb, L, A, nv, sn, sd);
+        __syncthreads();
+        flush_group<G>(dtile, sn, sd, tid, t0, nv, L.d0, D, N, dx + rowD, ddt + rowD, pbc);
+    }
+    cp_wait<0>();
+    store_dacc<G>(L, A, part_a, D, N);
 }
 
 // dB|dC = sum over the nblk CTA partials of each batch row (fixed order).
@@ -398,17 +673,27 @@ template <int G, bool VEC>
 static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaStream_t stream)
 {
     using S = BwdShape<G>;
-    cudaError_t e = cudaFuncSetAttribute(bwd_kernel<G, VEC>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
-    if (e != cudaSuccess) return e;
+    cudaError_t e;
     char *ws = static_cast<char *>(a.workspace);
     float *part_bc = reinterpret_cast<float *>(ws + w.part_bc);
     float *part_a = reinterpret_cast<float *>(ws + w.part_a);
     float *subck = reinterpret_cast<float *>(ws + w.subck);
     dim3 grid(w.nblk, a.Bt);
-    bwd_kernel<G, VEC><<<grid, BWD_THREADS, S::SMEM, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck,
-        a.T, a.D, a.N, a.K, w.nblk, w.nseg);
+    if (a.K == GRP) {
+        e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)S::SMEM_K8);
+        if (e != cudaSuccess) return e;
+        bwd_kernel_k8<G, VEC><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
+            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a,
+            a.T, a.D, a.N, w.nblk);
+    } else {
+        e = cudaFuncSetAttribute(bwd_kernel<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)S::SMEM);
+        if (e != cudaSuccess) return e;
+        bwd_kernel<G, VEC><<<grid, BWD_THREADS, S::SMEM, stream>>>(
+            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck,
+            a.T, a.D, a.N, a.K, w.nblk, w.nseg);
+    }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t nbc = (size_t)a.Bt * a.T * 2 * a.N;
     const int rb = (int)((nbc + 255) / 256 < 148 * 16 ? (nbc + 255) / 256 : 148 * 16);

@@ -75,13 +75,14 @@ def assert_parity(y, grads, y64, grads64, label=""):
         assert e <= GRAD_TOL, f"{label} {name}: normalised error {e:.3e} > {GRAD_TOL}"
 
 
+@pytest.mark.parametrize("chunk", [64, 8])
 @pytest.mark.parametrize("bt,t_len,d,n,dist", SHAPES)
-def test_forward_and_gradients_match_the_float64_oracle(bt, t_len, d, n, dist):
+def test_forward_and_gradients_match_the_float64_oracle(bt, t_len, d, n, dist, chunk):
     x, dt, aneg, b_in, c_in, dy = inputs(bt, t_len, d, n, dist, seed=SEED + d, device=DEV)
-    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy)
+    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
     assert y.shape == (bt, t_len, d) and y.dtype == torch.float32
-    y64, _, g64 = oracle64(x, dt, aneg, b_in, c_in, dy)
-    assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)}")
+    y64, _, g64 = oracle64(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)} chunk {chunk}")
 
 
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
@@ -128,7 +129,7 @@ def test_gradients_match_finite_differences():
     assert worst < 0.05, f"finite-difference mismatch: {worst:.3f}"
 
 
-@pytest.mark.parametrize("chunk", [1, 7, 64, 65, 100, 511, 512])
+@pytest.mark.parametrize("chunk", [1, 7, 8, 9, 16, 64, 65, 100, 511, 512])
 def test_checkpoint_stride_is_an_implementation_detail(chunk):
     """Reference gate (tests/test_scan.py:213-221), extended to the gradients."""
     x, dt, aneg, b_in, c_in, dy = inputs(2, 512, 96, 16, "ref", seed=SEED + 5, device=DEV)
