@@ -58,6 +58,9 @@ namespace mms {
 #ifndef MMS_BWD_MINB
 #define MMS_BWD_MINB 2
 #endif
+#ifndef MMS_BWD_K8_MINB
+#define MMS_BWD_K8_MINB 2
+#endif
 
 constexpr int BWD_THREADS = 256;
 constexpr int BWD_WARPS = BWD_THREADS / 32;
@@ -80,10 +83,10 @@ struct BwdShape {
     static constexpr int DERF = 3 * QF + 2 * PF;
     static constexpr int NV2 = 2 * NPAD;                   // dB|dC values per step per warp
     static constexpr size_t SLOTF = (size_t)SLOTS * BWD_THREADS * 4;
-    static constexpr size_t SNF = (size_t)GRP * DPB * G * 2;
-    static constexpr size_t SDF = (size_t)GRP * BWD_WARPS * NV2;
+    static constexpr size_t SDF = (size_t)GRP * BWD_WARPS * NV2;   // one of two buffers
+    static constexpr size_t CKF = (size_t)DPB * NPAD;            // entry-state slab of a group
     static constexpr size_t SMEM_K8 =
-        sizeof(float) * ((size_t)NAT_BUFS * NATF + (size_t)DER_BUFS * DERF + SNF + SDF);
+        sizeof(float) * ((size_t)NAT_BUFS * (NATF + CKF) + (size_t)DER_BUFS * DERF + 2 * SDF);
     static constexpr size_t SMEM = SMEM_K8 + sizeof(float) * SLOTF;
 };
 
@@ -218,6 +221,8 @@ struct Lane {
     using S = BwdShape<G>;
     int tid, lane, warp, g, c, d0, d, b, tau, pidx, u3, sd_pos;
     bool act, sd_writer;
+    bool n_ddt;          // after the sum over the channel's lanes this lane holds ddt (else dx)
+    bool n_writer;       // ... and stores it
     float2 an2[2];                                  // Aneg * log2(e) in lane state order
 
     __device__ Lane(const float *aneg, int D, int N) {
@@ -240,6 +245,8 @@ struct Lane {
         // (G <= 4: kind u3, state tau; G >= 8 writes several values).
         sd_pos = (G <= 4 ? u3 * S::NPAD : 0) + 4 * g + tau;
         sd_writer = G >= 4 || (lane & (G == 2 ? 2 : 3)) == 0;
+        n_ddt = G > 1 && (g & (G / 2)) != 0;
+        n_writer = d < D && (G == 1 || (g & (G / 2 - 1)) == 0);
         an2[0] = f2(0.f, 0.f);
         an2[1] = f2(0.f, 0.f);
         if (act) {
@@ -268,16 +275,26 @@ struct Adjoint {
     float2 dac[2];      // sum_t dt*g*dA*h_{t-1}
 };
 
-// Rebuild one group from the state entering it, then walk it backwards,
-// leaving the group's dx/ddt partials in sn and per-warp dB/dC sums in sd.
+// Rebuild one group from the state entering it, then walk it backwards:
+// dx/ddt are finished with shuffles across the channel's lanes and stored
+// (dxo/ddto point at this lane's channel at step t0), per-warp dB/dC sums go to sd.
+#ifndef MMS_WALK_KEEP_A
+#define MMS_WALK_KEEP_A 0
+#endif
+
 template <int G, bool FULL>
 __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&hb)[2],
                                            const Lane<G> &L, Adjoint &A, int nv,
-                                           float *sn, float *sd)
+                                           float *dxo, float *ddto, int D, float *sd)
 {
+    float *outp = L.n_ddt ? ddto : dxo;
     using S = BwdShape<G>;
-    constexpr int DPB = S::DPB, NPAD = S::NPAD, NV2 = S::NV2;
-    float2 av[GRP][2], hv[GRP][2];
+    constexpr int NPAD = S::NPAD, NV2 = S::NV2;
+    // Rebuild: the states of the group's steps (and, when kept, their decays).
+    float2 hv[GRP][2];
+#if MMS_WALK_KEEP_A
+    float2 av[GRP][2];
+#endif
 #pragma unroll
     for (int q = 0; q < GRP / 4; ++q) {
         const float4 x4 = v.x4(q), d4 = v.dt4(q);
@@ -287,12 +304,18 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
             const float dtv = comp(d4, k), bx = dtv * comp(x4, k);
             const float4 Bv = v.B(i);
             const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
-            av[i][0] = ex2x2(mul2(md, L.an2[0]));
-            av[i][1] = ex2x2(mul2(md, L.an2[1]));
-            hv[i][0] = fma2(av[i][0], i ? hv[i > 0 ? i - 1 : 0][0] : hb[0], mul2(bx2, lo(Bv)));
-            hv[i][1] = fma2(av[i][1], i ? hv[i > 0 ? i - 1 : 0][1] : hb[1], mul2(bx2, hi(Bv)));
+            const float2 a0 = ex2x2(mul2(md, L.an2[0]));
+            const float2 a1 = ex2x2(mul2(md, L.an2[1]));
+#if MMS_WALK_KEEP_A
+            av[i][0] = a0;
+            av[i][1] = a1;
+#endif
+            hv[i][0] = fma2(a0, i ? hv[i > 0 ? i - 1 : 0][0] : hb[0], mul2(bx2, lo(Bv)));
+            hv[i][1] = fma2(a1, i ? hv[i > 0 ? i - 1 : 0][1] : hb[1], mul2(bx2, hi(Bv)));
         }
     }
+    // Walk: acar carries dA of the step after the current one.
+    float2 acar[2] = {A.anx[0], A.anx[1]};
 #pragma unroll
     for (int q = GRP / 4 - 1; q >= 0; --q) {
         const float4 x4 = v.x4(q), d4 = v.dt4(q), y4 = v.dy4(q);
@@ -305,28 +328,42 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
             const float2 dy2 = f2(dyv, dyv), dt2 = f2(dtv, dtv);
             const float dxv = dtv * xv;
             const float2 dxv2 = f2(dxv, dxv);
+#if !MMS_WALK_KEEP_A
+            const float2 md = f2(-dtv, -dtv);
+#endif
             float2 p1 = f2(0.f, 0.f), p2 = f2(0.f, 0.f), vb[2], vc[2];
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-                float2 a1 = A.anx[p];
-                if (i + 1 < GRP) {
-                    const float2 an = av[i + 1 < GRP ? i + 1 : i][p];
-                    if (FULL) a1 = an;
-                    else if (i + 1 < nv) a1 = an;
-                }
+#if MMS_WALK_KEEP_A
+                const float2 ai = av[i][p];
+#else
+                const float2 am = mul2(md, L.an2[p]);
+                const float2 ai = f2(ex2_fresh(am.x), ex2_fresh(am.y));
+#endif
                 const float2 cp = p ? hi(Cv) : lo(Cv);
                 const float2 bp = p ? hi(Bv) : lo(Bv);
-                A.gad[p] = fma2(a1, A.gad[p], mul2(dy2, cp));
+                A.gad[p] = fma2(acar[p], A.gad[p], mul2(dy2, cp));
+                acar[p] = ai;
                 const float2 hp = i ? hv[i > 0 ? i - 1 : 0][p] : hb[p];
-                const float2 u = mul2(A.gad[p], mul2(av[i][p], hp));
+                const float2 u = mul2(A.gad[p], mul2(ai, hp));
                 p1 = fma2(A.gad[p], bp, p1);
                 p2 = fma2(L.an2[p], u, p2);
                 A.dac[p] = fma2(dt2, u, A.dac[p]);
                 vb[p] = mul2(A.gad[p], dxv2);
                 vc[p] = mul2(dy2, hv[i][p]);
             }
-            *reinterpret_cast<float2 *>(sn + ((i * DPB + L.c) * G + L.g) * 2) =
-                f2(p1.x + p1.y, p2.x + p2.y);
+            {   // dx = dt*sum_n g*B, ddt = x*sum_n g*B - sum_n Aneg*u (an2 carries log2 e)
+                const float s1 = p1.x + p1.y, s2 = p2.x + p2.y;
+                float vn[2] = {dtv * s1, fmaf(xv, s1, -MMS_LN2 * s2)};
+                if constexpr (G > 1) {
+                    int fn;
+                    transposed_reduce<2, G / 2, 1>(vn, L.lane, fn);
+                    if (L.n_writer) outp[(size_t)i * D] = vn[0];
+                } else if (L.n_writer) {
+                    dxo[(size_t)i * D] = vn[0];
+                    ddto[(size_t)i * D] = vn[1];
+                }
+            }
             // dB|dC butterfly across the warp's channels
             vb[0] = add2(vb[0], shfl2(vb[1], 16));
             vc[0] = add2(vc[0], shfl2(vc[1], 16));
@@ -354,33 +391,18 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
             }
         }
     }
-    A.anx[0] = av[0][0];
-    A.anx[1] = av[0][1];
+    A.anx[0] = acar[0];
+    A.anx[1] = acar[1];
 }
 
-// After a barrier: finish the group's sums. dx, ddt: one thread per (t, d),
-// coalesced stores. dB, dC: sum of the CTA's warps, this CTA's partial.
+// After a barrier: this CTA's partial of dB, dC for a walked group (the sum
+// over the CTA's warps of the per-warp butterfly results in sd).
 template <int G>
-__device__ __forceinline__ void flush_group(const float *dtile, const float *sn, const float *sd,
-                                            int tid, int t0, int nv, int d0, int D, int N,
-                                            float *dxb, float *ddtb, float *pbc)
+__device__ __forceinline__ void flush_group(const float *sd, int tid, int t0, int nv, int N,
+                                            float *pbc)
 {
     using S = BwdShape<G>;
-    constexpr int DPB = S::DPB, NPAD = S::NPAD, NV2 = S::NV2;
-    for (int p = tid; p < GRP * DPB; p += BWD_THREADS) {
-        const int i = p / DPB, cc = p % DPB;
-        if (i >= nv) break;
-        const float *src = sn + (size_t)p * G * 2;
-        float s1 = 0.f, s2 = 0.f;
-#pragma unroll
-        for (int q = 0; q < G; ++q) { s1 += src[2 * q]; s2 += src[2 * q + 1]; }
-        const int o = ((i >> 2) * DPB + cc) * 4 + (i & 3);
-        if (d0 + cc < D) {
-            const size_t go = (size_t)(t0 + i) * D + d0 + cc;
-            dxb[go] = dtile[S::QF + o] * s1;
-            ddtb[go] = fmaf(dtile[o], s1, -s2 * MMS_LN2);
-        }
-    }
+    constexpr int NPAD = S::NPAD, NV2 = S::NV2;
     for (int p = tid; p < GRP * NV2; p += BWD_THREADS) {
         const int i = p / NV2, jj = p % NV2;
         if (i >= nv) break;
@@ -421,9 +443,8 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     extern __shared__ __align__(16) float smem[];
     float *nat = smem;                                               // [NAT_BUFS][NATF]
     float *der = nat + NAT_BUFS * S::NATF;                           // [DER_BUFS][DERF]
-    float *sn = der + DER_BUFS * S::DERF;                            // [GRP][DPB][G][2]
-    float *sd = sn + S::SNF;                                         // [GRP][WARPS][NV2]
-    float4 *slots = reinterpret_cast<float4 *>(sd + S::SDF);         // [SLOTS][THREADS]
+    float *sd = der + DER_BUFS * S::DERF;                            // [2][GRP][WARPS][NV2]
+    float4 *slots = reinterpret_cast<float4 *>(sd + 2 * S::SDF);     // [SLOTS][THREADS]
 
     const Lane<G> L(aneg, D, N);
     const int tid = L.tid;
@@ -456,10 +477,15 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
     float2 hs[2];
     int cur_chunk = -1, cur_seg = -1;
+    int nw = 0, pend_t0 = 0, pend_nv = 0;            // walked groups; the one awaiting its flush
 
     for (int it = 0; !cur.done(); ++it, cur.advance()) {
         cp_wait<NAT_BUFS - 2>();                      // this thread's copies of item it+1
         __syncthreads();                              // everyone's copies; item it rewritten
+        if (pend_nv) {                                // dB|dC of the previous walked group
+            flush_group<G>(sd + ((nw - 1) & 1) * S::SDF, tid, pend_t0, pend_nv, N, pbc);
+            pend_nv = 0;
+        }
         {
             WorkCursor nxt = cur;
             nxt.advance();
@@ -527,12 +553,17 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             hb[0] = lo(w);
             hb[1] = hi(w);
         }
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, sn, sd);
-        else walk_group<G, false>(v, hb, L, A, nv, sn, sd);
-        __syncthreads();
-        flush_group<G>(dtile, sn, sd, tid, t0, nv, L.d0, D, N, dx + rowD, ddt + rowD, pbc);
+        float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
+        float *sdb = sd + (nw & 1) * S::SDF;
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        ++nw;
+        pend_t0 = t0;
+        pend_nv = nv;
     }
     cp_wait<0>();
+    __syncthreads();
+    if (pend_nv) flush_group<G>(sd + ((nw - 1) & 1) * S::SDF, tid, pend_t0, pend_nv, N, pbc);
     store_dacc<G>(L, A, part_a, D, N);
 }
 
@@ -540,7 +571,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 // entry state is the forward's checkpoint, so there is no recompute pass and
 // no slot storage; groups are simply chunks nchunk-1 .. 0.
 template <int G, bool VEC>
-__global__ void __launch_bounds__(BWD_THREADS, 2)
+__global__ void __launch_bounds__(BWD_THREADS, MMS_BWD_K8_MINB)
 bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
               const float *__restrict__ Cm, const float *__restrict__ dy,
@@ -553,8 +584,8 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     extern __shared__ __align__(16) float smem[];
     float *nat = smem;
     float *der = nat + NAT_BUFS * S::NATF;
-    float *sn = der + DER_BUFS * S::DERF;
-    float *sd = sn + S::SNF;
+    float *sd = der + DER_BUFS * S::DERF;               // [2][GRP][WARPS][NV2]
+    float *cks = sd + 2 * S::SDF;                      // [NAT_BUFS][DPB][NPAD] entry states
 
     const Lane<G> L(aneg, D, N);
     const int tid = L.tid;
@@ -566,21 +597,37 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     const float *ckb = ckpt + (size_t)L.b * nchunk * plane;
     float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
 
+    // Stage group c: its inputs and the checkpoint it starts from (zeros for c == 0).
+    auto stage = [&](int buf, int c) {
+        stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
+            nat + buf * S::NATF, xb, dtb, dyb, Bb, Cb, c * GRP, min(GRP, T - c * GRP),
+            L.d0, D, N, tid);
+        constexpr int QN = NPAD / 4;
+        for (int k = tid; k < DPB * QN; k += BWD_THREADS) {
+            const int cc = k / QN, q = k % QN;
+            const bool ok = c >= 1 && L.d0 + cc < D && 4 * q < N;
+            const float *src = ok ? ckb + (size_t)(c - 1) * plane + (size_t)(L.d0 + cc) * N + 4 * q
+                                  : ckb;
+            cp16(cks + buf * S::CKF + cc * NPAD + 4 * q, src, ok);
+        }
+    };
+    // The lane's 4 entry states (lane order) from a staged slab.
+    auto entry = [&](float2 (&h)[2], int buf) {
+        const float *p = cks + buf * S::CKF + L.c * NPAD + 4 * L.g;
+        h[0] = f2(p[0 ^ L.tau], p[1 ^ L.tau]);
+        h[1] = f2(p[2 ^ L.tau], p[3 ^ L.tau]);
+    };
+
 #pragma unroll
     for (int s = 0; s < NAT_BUFS; ++s) {
-        const int c = nchunk - 1 - s;
-        if (c >= 0)
-            stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
-                nat + s * S::NATF, xb, dtb, dyb, Bb, Cb, c * GRP, min(GRP, T - c * GRP),
-                L.d0, D, N, tid);
+        if (nchunk - 1 - s >= 0) stage(s, nchunk - 1 - s);
         cp_commit();
     }
-    float2 hnext[2];                                   // state entering the next group
-    if (nchunk >= 2) L.load_state(hnext, ckb + (size_t)(nchunk - 2) * plane, N);
-    else hnext[0] = hnext[1] = f2(0.f, 0.f);
     cp_wait<NAT_BUFS - 1>();
     __syncthreads();
     rewrite_tile<G>(nat, der, tid);
+    float2 hnext[2];                                   // state entering the current group
+    entry(hnext, 0);
 
     Adjoint A;
 #pragma unroll
@@ -590,30 +637,30 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const int c = nchunk - 1 - it;
         cp_wait<NAT_BUFS - 2>();
         __syncthreads();
-        if (c >= 1)
-            rewrite_tile<G>(nat + ((it + 1) % NAT_BUFS) * S::NATF,
-                            der + ((it + 1) % DER_BUFS) * S::DERF, tid);
-        if (c >= NAT_BUFS) {
-            const int cs = c - NAT_BUFS;
-            stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
-                nat + ((it + NAT_BUFS) % NAT_BUFS) * S::NATF, xb, dtb, dyb, Bb, Cb, cs * GRP,
-                GRP, L.d0, D, N, tid);
-        }
-        cp_commit();
+        if (it > 0)                                    // dB|dC of the group walked last
+            flush_group<G>(sd + ((it - 1) & 1) * S::SDF, tid, (c + 1) * GRP,
+                           min(GRP, T - (c + 1) * GRP), N, pbc);
         const float2 hb[2] = {hnext[0], hnext[1]};
-        if (c >= 2) L.load_state(hnext, ckb + (size_t)(c - 2) * plane, N);
-        else hnext[0] = hnext[1] = f2(0.f, 0.f);
+        if (c >= 1) {                                  // group it+1: rewrite, take its entry state
+            const int nb = (it + 1) % NAT_BUFS;
+            rewrite_tile<G>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid);
+            entry(hnext, nb);
+        }
+        if (c >= NAT_BUFS) stage((it + NAT_BUFS) % NAT_BUFS, c - NAT_BUFS);
+        cp_commit();
 
         const float *dtile = der + (it % DER_BUFS) * S::DERF;
         const TileView<G> v(dtile, L.c, L.g, L.pidx);
         const int t0 = c * GRP;
         const int nv = min(GRP, T - t0);
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, sn, sd);
-        else walk_group<G, false>(v, hb, L, A, nv, sn, sd);
-        __syncthreads();
-        flush_group<G>(dtile, sn, sd, tid, t0, nv, L.d0, D, N, dx + rowD, ddt + rowD, pbc);
+        float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
+        float *sdb = sd + (it & 1) * S::SDF;
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
     }
     cp_wait<0>();
+    __syncthreads();
+    flush_group<G>(sd + ((nchunk - 1) & 1) * S::SDF, tid, 0, min(GRP, T), N, pbc);
     store_dacc<G>(L, A, part_a, D, N);
 }
 

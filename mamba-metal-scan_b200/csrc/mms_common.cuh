@@ -17,6 +17,14 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Same, but never merged with an identical ex2 elsewhere: used where a decay
+// is deliberately recomputed instead of being kept in a register.
+__device__ __forceinline__ float ex2_fresh(float x) {
+    float y;
+    asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ float4 ld4(const float *p) {
     return __ldg(reinterpret_cast<const float4 *>(p));
 }
