@@ -47,6 +47,8 @@ extern "C" {
 #define MMS_ERR_WORKSPACE 3        /* workspace NULL or smaller than required           */
 #define MMS_ERR_MISALIGNED 4       /* a pointer violates the alignment rules above      */
 #define MMS_ERR_CUDA 5             /* a kernel launch failed (see cudaGetLastError)      */
+#define MMS_ERR_TOO_LARGE 6        /* mms_bwd_noalloc: the shape needs more scratch than
+                                      MMS_NOALLOC_SCRATCH_BYTES                          */
 
 /* Version of the ABI in this header (major * 100 + minor). */
 #define MMS_ABI_VERSION 100
@@ -86,6 +88,29 @@ int mms_bwd(const float *x, const float *dt, const float *aneg,
             float *dx, float *ddt, float *daneg, float *dB, float *dC,
             void *workspace, size_t workspace_bytes,
             int Bt, int T, int D, int N, int K, void *stream);
+
+/*
+ * Backward scan that allocates nothing, for callers that cannot allocate
+ * device memory at run time (a plugin inside a host framework that has
+ * reserved all GPU memory and forbids further cudaMalloc, or a latency-bound
+ * path that cannot afford cudaMalloc's implicit device synchronisation).
+ * No counterpart in the reference: it is mms_bwd() with its workspace taken
+ * from MMS_NOALLOC_SCRATCH_BYTES of static device memory compiled into the
+ * library, held by every GPU that loads the library until the process exits.
+ *  - Shapes with mms_bwd_workspace_size() > MMS_NOALLOC_SCRATCH_BYTES return
+ *    MMS_ERR_TOO_LARGE (nothing is launched).
+ *  - The first call on a device looks the scratch address up (cudaGetSymbolAddress,
+ *    with that device current); make that first call before any stream capture.
+ *  - All calls share the one scratch array: calls that overlap on the GPU
+ *    (other streams, unordered host threads) race and must be serialised.
+ *    Nothing in it needs clearing between calls.
+ * Other arguments, outputs and status codes are those of mms_bwd().
+ */
+#define MMS_NOALLOC_SCRATCH_BYTES ((size_t)16 << 20)
+int mms_bwd_noalloc(const float *x, const float *dt, const float *aneg,
+                    const float *B, const float *C, const float *dy, const float *ckpt,
+                    float *dx, float *ddt, float *daneg, float *dB, float *dC,
+                    int Bt, int T, int D, int N, int K, void *stream);
 
 #ifdef __cplusplus
 }

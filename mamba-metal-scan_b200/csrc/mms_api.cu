@@ -37,6 +37,9 @@ const char *mms_status_string(int status)
     case MMS_ERR_WORKSPACE: return "workspace missing or smaller than mms_bwd_workspace_size()";
     case MMS_ERR_MISALIGNED: return "misaligned pointer (B, C, Aneg, ckpt, dB, dC, dAneg need 16 bytes)";
     case MMS_ERR_CUDA: return "CUDA launch failed";
+    case MMS_ERR_TOO_LARGE:
+        return "shape needs more workspace than mms_bwd_noalloc's static scratch "
+               "(MMS_NOALLOC_SCRATCH_BYTES = 16 MiB); use mms_bwd with a caller workspace";
     default: return "unknown status";
     }
 }

@@ -21,6 +21,7 @@ MMS_ERR_UNSUPPORTED_N = 2
 MMS_ERR_WORKSPACE = 3
 MMS_ERR_MISALIGNED = 4
 MMS_ERR_CUDA = 5
+MMS_ERR_TOO_LARGE = 6
 
 # Every symbol include/mms_scan.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -31,6 +32,7 @@ SIGNATURES = {
     "mms_fwd": ([_P] * 7 + [_I] * 5 + [_P], _I),
     "mms_bwd_workspace_size": ([_I] * 5, ctypes.c_size_t),
     "mms_bwd": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
+    "mms_bwd_noalloc": ([_P] * 12 + [_I] * 5 + [_P], _I),
 }
 
 _lib = None
