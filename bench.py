@@ -5,7 +5,8 @@
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 One step = forward + backward of the scan over one batch at BASELINE config 1
-(B=16, T=512, d_inner=2304, d_state=16, checkpoint stride 64) per GPU, with
+(B=16, T=512, d_inner=2304, d_state=16) per GPU, at the package's default
+checkpoint stride (8; the reference's 64 is timed alongside), with
 seeded synthetic inputs of the configs' distributions. With N GPUs every rank
 scans its own batch (batch sharding, no collective: weak scaling) and `value`
 is the total elements of all ranks over the slowest rank's device time.
@@ -48,10 +49,10 @@ N_SM = 148
 
 CONFIGS = {
     # name: (B, T, D, N, K)
-    "c1": (16, 512, 2304, 16, 64),
-    "c3a": (1, 16384, 2048, 16, 64),     # one sequence of config 3 per GPU
-    "c3b": (1, 16384, 2048, 64, 64),
-    "c4": (4, 4096, 8192, 16, 64),
+    "c1": (16, 512, 2304, 16, 8),
+    "c3a": (1, 16384, 2048, 16, 8),      # one sequence of config 3 per GPU
+    "c3b": (1, 16384, 2048, 64, 8),
+    "c4": (4, 4096, 8192, 16, 8),
 }
 
 
@@ -345,6 +346,9 @@ def run_native(args, shape):
         "gpu_launches": 4 * K,
     }
 
+    if kk != 64:
+        line["reference_stride"] = time_stride(lib, _native, shape[:4] + (64,), device,
+                                               (x, dt, aneg, b_in, c_in, dy), stream)
     # e2e through the public API from pinned host buffers
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan)
@@ -356,6 +360,43 @@ def run_native(args, shape):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def time_stride(lib, _native, shape, device, ins, stream, k=20):
+    """fwd and bwd kernel times at another checkpoint stride (same inputs)."""
+    bt, t_len, d, n, kk = shape
+    x, dt, aneg, b_in, c_in, dy = ins
+    P = lambda t: t.data_ptr()  # noqa: E731
+    y = torch.empty_like(x)
+    ckpt = torch.empty(bt, (t_len + kk - 1) // kk, d, n, device=device)
+    grads = [torch.empty_like(x), torch.empty_like(x), torch.empty_like(aneg),
+             torch.empty_like(b_in), torch.empty_like(c_in)]
+    nb = _native.bwd_workspace_size(bt, t_len, d, n, kk)
+    ws = torch.empty(nb, dtype=torch.uint8, device=device)
+    sp = stream.cuda_stream
+
+    def fwd():
+        lib.mms_fwd(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(y), P(ckpt), bt, t_len, d, n, kk, sp)
+
+    def bwd():
+        lib.mms_bwd(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(dy), P(ckpt), *(P(g) for g in grads),
+                    P(ws), nb, bt, t_len, d, n, kk, sp)
+
+    for _ in range(3):
+        fwd()
+        bwd()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record(stream)
+    for _ in range(k):
+        fwd()
+    ev[1].record(stream)
+    for _ in range(k):
+        bwd()
+    ev[2].record(stream)
+    torch.cuda.synchronize()
+    f, b = ev[0].elapsed_time(ev[1]) / k, ev[1].elapsed_time(ev[2]) / k
+    return {"chunk": kk, "fwd_ms": f, "bwd_ms": b, "value": bt * t_len * d / ((f + b) * 1e-3),
+            "unit": UNIT, "note": "the reference's checkpoint stride, same inputs, kernels only"}
 
 
 def run_e2e(args, shape, device, world, rank, selective_scan):
@@ -436,7 +477,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
-    ap.add_argument("--chunk", type=int, default=None, help="checkpoint stride (default 64)")
+    ap.add_argument("--chunk", type=int, default=None, help="checkpoint stride (default: the config's, 8)")
     ap.add_argument("--cpu-budget", type=float, default=10.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true")

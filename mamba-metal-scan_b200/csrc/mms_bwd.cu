@@ -137,13 +137,6 @@ struct WorkCursor {
     __device__ int nvalid() const { return phase == 0 ? GRP : min(GRP, u1 - (u0 + j * GRP)); }
 };
 
-__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 ex2x2(float2 v) { return f2(ex2(v.x), ex2(v.y)); }
-__device__ __forceinline__ float2 lo(float4 v) { return f2(v.x, v.y); }
-__device__ __forceinline__ float2 hi(float4 v) { return f2(v.z, v.w); }
 __device__ __forceinline__ float2 shfl2(float2 v, int m) {
     return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }

@@ -37,6 +37,15 @@ __device__ __forceinline__ float comp(const float4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
 
+// Packed fp32 pairs: sm_100's FFMA2/FMUL2/FADD2 do two lanes of work per issue.
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ex2x2(float2 v) { return f2(ex2(v.x), ex2(v.y)); }
+__device__ __forceinline__ float2 lo(float4 v) { return f2(v.x, v.y); }
+__device__ __forceinline__ float2 hi(float4 v) { return f2(v.z, v.w); }
+
 // Transposed butterfly reduction over the lanes selected by lane-bit masks
 // MASK_HI, MASK_HI/2, ..., MASK_LO (powers of two). Each lane starts with NV
 // values v[0..NV); lanes that differ only in those bits hold partials of the

@@ -57,13 +57,14 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     const bool act = d < D && 4 * g < N;
     const int nchunk = (T + K - 1) / K;
 
-    float an2[4] = {0.f, 0.f, 0.f, 0.f};                   // Aneg * log2(e)
+    // -Aneg * log2(e) as two packed pairs: dA = 2^(dt * nan2).
+    float2 nan2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
     if (act) {
         const float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
-        an2[0] = a4.x * MMS_LOG2E; an2[1] = a4.y * MMS_LOG2E;
-        an2[2] = a4.z * MMS_LOG2E; an2[3] = a4.w * MMS_LOG2E;
+        nan2[0] = f2(-a4.x * MMS_LOG2E, -a4.y * MMS_LOG2E);
+        nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
-    float h[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 h[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 
     const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
@@ -102,17 +103,14 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             const float dtv = row[DPB + c];
             const float4 Bv = *reinterpret_cast<const float4 *>(row + 2 * DPB + 4 * g);
             const float4 Cv = *reinterpret_cast<const float4 *>(row + 2 * DPB + NPAD + 4 * g);
-            const float ml = -dtv, bx = dtv * xv;
-            float acc = 0.f;
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const float a = ex2(ml * an2[s]);
-                h[s] = fmaf(a, h[s], bx * comp(Bv, s));
-                acc = fmaf(comp(Cv, s), h[s], acc);
-            }
-            ys[(j * DPB + c) * G + g] = acc;
+            const float bx = dtv * xv;
+            const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
+            h[0] = fma2(ex2x2(mul2(dt2, nan2[0])), h[0], mul2(bx2, lo(Bv)));
+            h[1] = fma2(ex2x2(mul2(dt2, nan2[1])), h[1], mul2(bx2, hi(Bv)));
+            const float2 acc = fma2(hi(Cv), h[1], mul2(lo(Cv), h[0]));
+            ys[(j * DPB + c) * G + g] = acc.x + acc.y;
             if (t0 + j == next_ck) {                       // uniform across the CTA
-                if (act) st4(ckb + (size_t)chunk * D * N, make_float4(h[0], h[1], h[2], h[3]));
+                if (act) st4(ckb + (size_t)chunk * D * N, make_float4(h[0].x, h[0].y, h[1].x, h[1].y));
                 ++chunk;
                 next_ck = min(next_ck + K, T - 1);
             }
