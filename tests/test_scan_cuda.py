@@ -85,6 +85,22 @@ def test_forward_and_gradients_match_the_float64_oracle(bt, t_len, d, n, dist, c
     assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)} chunk {chunk}")
 
 
+# Shapes with B*D large enough for the forward's whole-state kernel (one thread
+# per channel, d_state 12 or 16), with aligned and unaligned D.
+WIDE = [(2, 130, 9500, 16, 8), (2, 77, 9501, 12, 64), (1, 300, 19000, 16, 7)]
+
+
+@pytest.mark.parametrize("bt,t_len,d,n,chunk", WIDE)
+def test_wide_channel_counts_match_the_float64_oracle(bt, t_len, d, n, chunk):
+    x, dt, aneg, b_in, c_in, dy = inputs(bt, t_len, d, n, "c0", seed=d, device=DEV)
+    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    y64, ckpt64, g64 = oracle64(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)} chunk {chunk}")
+    from mamba_metal import _native
+    _, ckpt = _native.fwd(x, dt, aneg, b_in, c_in, chunk)
+    assert max_rel(ckpt, ckpt64) <= FWD_TOL
+
+
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
 def test_golden_vectors_from_the_reference(path):
     """The reference's own outputs (fp32 and fp64), recorded by tests/golden/make_golden.py."""
