@@ -313,7 +313,8 @@ def run_native(args, shape):
     traffic = None
     tfile = REPO / "profiles" / "traffic.json"
     if tfile.exists():
-        traffic = json.loads(tfile.read_text()).get(f"{args.config}_bwd_bytes_per_launch")
+        if kk == 8:           # the capture was taken at the default stride
+            traffic = json.loads(tfile.read_text()).get(f"{args.config}_bwd_bytes_per_launch")
     sm_mhz = clk.get("sm_mhz") or sm_max_default
     exps = 2 * elems * n
     t_hbm = (fwd_b + bwd_b) / (hbm_gbs * 1e9)
@@ -346,7 +347,7 @@ def run_native(args, shape):
         "gpu_launches": 4 * K,
     }
 
-    if kk != 64:
+    if kk != 64 and not args.no_stride64:
         line["reference_stride"] = time_stride(lib, _native, shape[:4] + (64,), device,
                                                (x, dt, aneg, b_in, c_in, dy), stream)
     # e2e through the public API from pinned host buffers
@@ -483,6 +484,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-stride64", action="store_true",
+                    help="skip the side timing at the reference's checkpoint stride")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)         # the timing rules ask for at least 3
     shape = CONFIGS[args.config]
