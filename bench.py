@@ -19,6 +19,7 @@ Printed (rank 0): one JSON line with the contract keys plus
   e2e           the public API (selective_scan + autograd) from pinned host
                 buffers, copies in and all outputs back inside the timed region
   train         TinyMamba config 2 (vocab 32768, d_model 640, 12 layers) tok/s
+  decode        the one-token step kernel at the config-4 decode shape
   clocks        nvidia-smi samples taken during the timed region
 `--impl reference` times only the reference CPU path (rank 0) and prints its line.
 """
@@ -253,13 +254,25 @@ def run_native(args, shape):
         dist.init_process_group("nccl", device_id=device,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     lib = _native.load()
-    bt, t_len, d, n, kk = shape
-    x, dt, aneg, b_in, c_in, dy = make_inputs(bt, t_len, d, n, 1000 + rank, device)
+    bt, t_len, d_total, n, kk = shape
+    channel = args.shard == "channel" and world > 1
+    if channel:
+        # this rank's channels; B and C are the same on every rank (same seed)
+        from mamba_metal.sharded import channel_shard
+        sl = channel_shard(d_total, world, rank)
+        x, dt, aneg, b_in, c_in, dy = make_inputs(bt, t_len, d_total, n, 1000, device)
+        x, dt, dy = (t[:, :, sl].contiguous() for t in (x, dt, dy))
+        aneg = aneg[sl].contiguous()
+    else:
+        x, dt, aneg, b_in, c_in, dy = make_inputs(bt, t_len, d_total, n, 1000 + rank, device)
+    d = x.shape[2]
     nchunk = (t_len + kk - 1) // kk
     y = torch.empty_like(x)
     ckpt = torch.empty(bt, nchunk, d, n, device=device)
     dx, ddt = torch.empty_like(x), torch.empty_like(x)
-    daneg, db, dc = torch.empty_like(aneg), torch.empty_like(b_in), torch.empty_like(c_in)
+    daneg = torch.empty_like(aneg)
+    dbc = torch.empty(2, bt, t_len, n, device=device)     # packed [dB | dC]
+    db, dc = dbc[0], dbc[1]
     ws_bytes = _native.bwd_workspace_size(bt, t_len, d, n, kk)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=device)
     stream = torch.cuda.current_stream(device)
@@ -276,6 +289,8 @@ def run_native(args, shape):
                          P(dx), P(ddt), P(daneg), P(db), P(dc), P(ws), ws_bytes,
                          bt, t_len, d, n, kk, sp)
         assert rc == 0, _native.status_string(rc)
+        if channel:       # dB, dC are partial sums over this rank's channels
+            dist.all_reduce(dbc, op=dist.ReduceOp.SUM)
 
     for _ in range(args.warmup):
         fwd()
@@ -303,7 +318,8 @@ def run_native(args, shape):
     fwd_ms = statistics.mean(e[0].elapsed_time(e[1]) for e in ev)
     bwd_ms = statistics.mean(e[1].elapsed_time(e[2]) for e in ev)
     elems = bt * t_len * d
-    value = world * elems * K / (t_ms * 1e-3)
+    total_elems = bt * t_len * d_total if channel else world * elems
+    value = total_elems * K / (t_ms * 1e-3)
     ms_per_step = t_ms / K
 
     hbm_gbs, peak_kind, sm_max_default = measured_peaks()
@@ -324,10 +340,15 @@ def run_native(args, shape):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d} N{n} K{kk} per GPU",
-                   "batch_per_gpu": bt, "seq_len": t_len, "d_inner": d, "d_state": n, "chunk": kk,
-                   "parallelism": f"batch-shard x{world} (no collective)",
+        "scaling": "strong" if channel else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": (f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d_total} N{n} K{kk}, "
+                                f"d_inner sharded {d} per GPU" if channel else
+                                f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d} N{n} K{kk} per GPU"),
+                   "batch_per_gpu": bt, "seq_len": t_len, "d_inner": d_total, "d_state": n, "chunk": kk,
+                   "parallelism": (f"d_inner-shard x{world} + NCCL all-reduce of packed [dB|dC] "
+                                   f"({2 * bt * t_len * n * 4} B)" if channel else
+                                   f"batch-shard x{world} (no collective)"),
                    "l2": "inputs larger than L2 (%.0f MB touched per step)" % ((fwd_b + bwd_b) / 1e6)},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
         "roofline": {"kernel": "mms_bwd (bwd_kernel + 2 reduce kernels)", "bound": "hbm",
@@ -348,13 +369,15 @@ def run_native(args, shape):
     }
 
     if kk != 64 and not args.no_stride64:
-        line["reference_stride"] = time_stride(lib, _native, shape[:4] + (64,), device,
+        line["reference_stride"] = time_stride(lib, _native, (bt, t_len, d, n, 64), device,
                                                (x, dt, aneg, b_in, c_in, dy), stream)
     # e2e through the public API from pinned host buffers
     if not args.no_e2e:
-        line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan)
+        line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan, channel)
     if not args.no_train and world == 1:
         line["train"] = run_train(args, device)
+    if not args.no_decode and world == 1:
+        line["decode"] = run_decode(args, device, hbm_gbs)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(shape, args.cpu_budget)
     if rank == 0:
@@ -400,9 +423,19 @@ def time_stride(lib, _native, shape, device, ins, stream, k=20):
             "unit": UNIT, "note": "the reference's checkpoint stride, same inputs, kernels only"}
 
 
-def run_e2e(args, shape, device, world, rank, selective_scan):
-    bt, t_len, d, n, kk = shape
-    host = [t.pin_memory() for t in make_inputs(bt, t_len, d, n, 2000 + rank, "cpu")]
+def run_e2e(args, shape, device, world, rank, selective_scan, channel=False):
+    bt, t_len, d_total, n, kk = shape
+    host = make_inputs(bt, t_len, d_total, n, 2000 + (0 if channel else rank), "cpu")
+    if channel:
+        from mamba_metal.sharded import channel_shard, selective_scan_channel_sharded
+        sl = channel_shard(d_total, world, rank)
+        host = [t[:, :, sl] if t.dim() == 3 and t.shape[2] == d_total else t for t in host]
+        host[2] = host[2][sl]
+        scan = lambda *a: selective_scan_channel_sharded(*a, impl="cuda", chunk=kk)  # noqa: E731
+    else:
+        scan = lambda *a: selective_scan(*a, impl="cuda", chunk=kk)  # noqa: E731
+    host = [t.contiguous().pin_memory() for t in host]
+    d = host[0].shape[2]
     outs_h = [torch.empty(bt, t_len, d).pin_memory() for _ in range(3)] + \
              [torch.empty(d, n).pin_memory(), torch.empty(bt, t_len, n).pin_memory(),
               torch.empty(bt, t_len, n).pin_memory()]
@@ -413,7 +446,7 @@ def run_e2e(args, shape, device, world, rank, selective_scan):
     def step():
         x, dt, aneg, b_in, c_in, dy = (t.to(device, non_blocking=True) for t in host)
         leaves = [t.requires_grad_(True) for t in (x, dt, aneg, b_in, c_in)]
-        y = selective_scan(*leaves, impl="cuda", chunk=kk)
+        y = scan(*leaves)
         grads = torch.autograd.grad(y, leaves, grad_outputs=dy)
         for dst, src in zip(outs_h, (y.detach(),) + grads):
             dst.copy_(src, non_blocking=True)
@@ -431,7 +464,8 @@ def run_e2e(args, shape, device, world, rank, selective_scan):
     e.record(stream)
     torch.cuda.synchronize()
     t_ms = max_over_ranks(s.elapsed_time(e), world, device)
-    return {"value": world * bt * t_len * d * k / (t_ms * 1e-3), "unit": UNIT,
+    total = bt * t_len * d_total if channel else world * bt * t_len * d
+    return {"value": total * k / (t_ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": k,
             "api": "mamba_metal.selective_scan(impl='cuda') + torch.autograd.grad, pinned host I/O"}
 
@@ -471,6 +505,66 @@ def run_train(args, device):
                       "batch 16 x seq 512, fp32, AdamW; scan on the CUDA kernels"}
 
 
+def run_decode(args, device, hbm_gbs):
+    """Config-4 decode case: mms_step at B=256, d_inner=2304, d_state=16, 128 steps.
+
+    Each step runs over 12 layers' caches in turn (TinyMamba's layer count), so
+    the 12 x 37.7 MB of state exceed L2 and every launch reads its state from
+    HBM, as in a real decode. The loop of 128 x 12 launches is captured once in
+    a CUDA graph and replayed; the graph is timed with CUDA events.
+    """
+    from mamba_metal import _native
+    lib = _native.load()
+    bt, d, n, steps, layers = 256, 2304, 16, 128, 12
+    g = torch.Generator(device="cpu").manual_seed(7)
+    xs = torch.randn(steps, bt, d, generator=g).to(device)
+    dts = torch.nn.functional.softplus(-2.0 + 0.5 * torch.randn(steps, bt, d, generator=g)).to(device)
+    bs = torch.randn(steps, bt, n, generator=g).to(device)
+    cs = torch.randn(steps, bt, n, generator=g).to(device)
+    anegs = [(torch.arange(1, n + 1).float() * (1 + 0.1 * torch.rand(d, n, generator=g))).to(device)
+             for _ in range(layers)]
+    hs = [torch.zeros(bt, d, n, device=device) for _ in range(layers)]
+    ys = torch.empty(steps, layers, bt, d, device=device)
+    P = lambda t: t.data_ptr()  # noqa: E731
+
+    def loop(sp):
+        for t in range(steps):
+            for li in range(layers):
+                rc = lib.mms_step(P(xs[t]), P(dts[t]), P(anegs[li]), P(bs[t]), P(cs[t]), P(hs[li]),
+                                  P(ys[t, li]), bt, d, n, sp)
+                assert rc == 0, _native.status_string(rc)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        loop(side.cuda_stream)                     # warm-up, eager
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        loop(torch.cuda.current_stream(device).cuda_stream)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = 5
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        graph.replay()
+    e.record()
+    torch.cuda.synchronize()
+    launches = reps * steps * layers
+    us = s.elapsed_time(e) * 1e3 / launches
+    nbytes = 8 * bt * d * n + 12 * bt * d + 8 * bt * n + 4 * d * n
+    del graph
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"workload": f"decode: mms_step B{bt} D{d} N{n}, {steps} steps x {layers} layer caches "
+                        "(CUDA graph)", "us_per_step": us,
+            "tokens_per_s_per_layer": bt / (us * 1e-6),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": gbs / hbm_gbs, "algorithmic_bytes_per_launch": nbytes},
+            "gpu_launches": launches}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -484,11 +578,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode-step timing")
+    ap.add_argument("--shard", choices=("batch", "channel"), default=None,
+                    help="multi-GPU split (default: channel for c4, batch otherwise)")
     ap.add_argument("--no-stride64", action="store_true",
                     help="skip the side timing at the reference's checkpoint stride")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)         # the timing rules ask for at least 3
     shape = CONFIGS[args.config]
+    if args.shard is None:
+        args.shard = "channel" if args.config == "c4" else "batch"
     if args.chunk:
         shape = shape[:4] + (args.chunk,)
     if args.impl == "reference":

@@ -112,6 +112,21 @@ int mms_bwd_noalloc(const float *x, const float *dt, const float *aneg,
                     float *dx, float *ddt, float *daneg, float *dB, float *dC,
                     int Bt, int T, int D, int N, int K, void *stream);
 
+/*
+ * One recurrent (decode) step on a cached state, in place:
+ *     h[b,d,n] = exp(-dt[b,d] * Aneg[d,n]) * h[b,d,n] + dt[b,d] * B[b,n] * x[b,d]
+ *     y[b,d]   = sum_n C[b,n] * h[b,d,n]            (with the updated h)
+ * Layouts: x, dt, y (Bt, D); B, C (Bt, N); Aneg (D, N); h (Bt, D, N), which
+ * is the layout of ckpt's last chunk, so the forward's final checkpoint can
+ * be the cache. h must not overlap any other argument. Alignment and N rules
+ * as above (h: 16 bytes).
+ * Replaces the reference's per-token torch ops on cache["h"]
+ * (mamba_metal/model.py:228-241), which have no kernel of their own there.
+ */
+int mms_step(const float *x, const float *dt, const float *aneg,
+             const float *B, const float *C, float *h, float *y,
+             int Bt, int D, int N, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,4 +85,19 @@ int mms_bwd(const float *x, const float *dt, const float *aneg, const float *B, 
                                                                                  : MMS_ERR_CUDA;
 }
 
+int mms_step(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
+             float *h, float *y, int Bt, int D, int N, void *stream)
+{
+    int rc = check_shape(Bt, 1, D, N, 1);
+    if (rc) return rc;
+    if ((long long)Bt * D * N > (1LL << 40)) return MMS_ERR_INVALID_ARG;
+    if (!x || !dt || !aneg || !B || !C || !h || !y) return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(h, 16) ||
+        !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
+        return MMS_ERR_MISALIGNED;
+    mms::StepArgs a{x, dt, aneg, B, C, h, y, Bt, D, N};
+    return mms::launch_step(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                  : MMS_ERR_CUDA;
+}
+
 }  // extern "C"

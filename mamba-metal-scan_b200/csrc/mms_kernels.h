@@ -20,6 +20,12 @@ struct BwdArgs {
     int Bt, T, D, N, K;
 };
 
+struct StepArgs {
+    const float *x, *dt, *aneg, *B, *C;
+    float *h, *y;
+    int Bt, D, N;
+};
+
 // Lanes per channel: ceil(N/4) rounded up to a power of two (N in [4, 64]).
 inline int groups_for(int N)
 {
@@ -52,5 +58,6 @@ BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K);
 
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream);
+cudaError_t launch_step(const StepArgs &a, cudaStream_t stream);
 
 }  // namespace mms

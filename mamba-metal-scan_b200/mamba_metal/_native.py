@@ -33,6 +33,7 @@ SIGNATURES = {
     "mms_bwd_workspace_size": ([_I] * 5, ctypes.c_size_t),
     "mms_bwd": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
     "mms_bwd_noalloc": ([_P] * 12 + [_I] * 5 + [_P], _I),
+    "mms_step": ([_P] * 7 + [_I] * 3 + [_P], _I),
 }
 
 _lib = None
@@ -116,3 +117,15 @@ def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None):
                      bt, t_len, d, n, chunk, _stream(x.device))
     _check(rc, "mms_bwd")
     return dx, ddt, daneg, db, dc
+
+
+def step(x, dt, aneg, b_in, c_in, h):
+    """One decode step: updates h (B,D,N) in place, returns y (B,D)."""
+    lib = load()
+    bt, d = x.shape
+    n = aneg.shape[1]
+    y = torch.empty(bt, d, device=x.device, dtype=torch.float32)
+    rc = lib.mms_step(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(h), _ptr(y),
+                      bt, d, n, _stream(x.device))
+    _check(rc, "mms_step")
+    return y

@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from mamba_metal.scan import selective_scan
+from mamba_metal.scan import selective_scan, selective_scan_step, selective_scan_step_ref
 
 
 @dataclass
@@ -195,6 +195,26 @@ class MambaBlock(nn.Module):
         y = (h * C_t.unsqueeze(2)).sum(-1)
         return (y, h[:, -1]) if return_state else y
 
+    def _step(self, x, dt, Aneg, B_t, C_t, cache):
+        """One token of the recurrence on cache["h"]; y (B, d_inner).
+
+        Without autograd, on CUDA, the fused decode kernel updates the cached
+        state in place (it owns that buffer: the scan's returned state is a
+        detached checkpoint). With autograd, or off-CUDA, the step is the
+        reference's differentiable PyTorch ops and the cache gets a new tensor.
+        """
+        h = cache["h"]
+        needs_grad = torch.is_grad_enabled() and any(
+            t.requires_grad for t in (x, dt, Aneg, B_t, C_t, h))
+        if x.is_cuda and self.scan_impl != "torch" and not needs_grad:
+            if not cache.get("h_owned"):
+                h = h.clone(memory_format=torch.contiguous_format)
+                cache["h"], cache["h_owned"] = h, True
+            return selective_scan_step(x, dt, Aneg, B_t, C_t, h, impl=self.scan_impl)
+        y, cache["h"] = selective_scan_step_ref(x, dt, Aneg, B_t, C_t, h)
+        cache["h_owned"] = False
+        return y
+
     def forward(self, x, cache=None):
         residual = x
         x, z = self.in_proj(self.norm(x)).chunk(2, dim=-1)
@@ -205,11 +225,7 @@ class MambaBlock(nn.Module):
             x = F.silu(self.conv(window)[:, :, kc - 1:kc]).transpose(1, 2)
             cache["conv"] = window[:, :, 1:]
             dt, B_t, C_t, Aneg = self._proj(x)
-            a = torch.exp(-dt.unsqueeze(-1) * Aneg)[:, 0]                  # (B, d_inner, N)
-            b = (dt.unsqueeze(-1) * B_t.unsqueeze(2) * x.unsqueeze(-1))[:, 0]
-            h = cache["h"] * a + b
-            cache["h"] = h
-            y = (h.unsqueeze(1) * C_t.unsqueeze(2)).sum(-1)                 # (B, 1, d_inner)
+            y = self._step(x[:, 0], dt[:, 0], Aneg, B_t[:, 0], C_t[:, 0], cache).unsqueeze(1)
         else:
             xc = x.transpose(1, 2)
             x = F.silu(self.conv(xc)[:, :, :xc.shape[2]]).transpose(1, 2)
@@ -221,7 +237,7 @@ class MambaBlock(nn.Module):
             # the last checkpoint of the scan is h[:, -1]: the cache costs nothing
             y, h_last = self._scan(x, return_state=True)
             if cache is not None:
-                cache["h"] = h_last
+                cache["h"], cache["h_owned"] = h_last, False
         y = y + self.D_skip
         return residual + self.out_proj(y * F.silu(z))
 

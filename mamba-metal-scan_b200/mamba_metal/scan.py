@@ -192,3 +192,61 @@ def selective_scan(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
         raise RuntimeError(f"scan_impl={impl!r} needs CUDA tensors (this build has no MPS/Metal "
                            f"backend); got device {x.device.type!r}")
     return None
+
+
+# ------------------------------------------------------------ decode (one token)
+
+def selective_scan_step_ref(x, dt, aneg, b_in, c_in, h):
+    """One recurrent step in PyTorch ops (reference model.py:228-241).
+
+    x, dt (B, D); B, C (B, N); Aneg (D, N); h (B, D, N). Returns (y (B, D),
+    new h); h itself is not modified.
+    """
+    dt_ = dt.unsqueeze(-1)
+    h = h * torch.exp(-dt_ * aneg) + dt_ * b_in.unsqueeze(1) * x.unsqueeze(-1)
+    return (h * c_in.unsqueeze(1)).sum(-1), h
+
+
+def selective_scan_step(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                        b_in: torch.Tensor, c_in: torch.Tensor, h: torch.Tensor,
+                        impl: str = "auto"):
+    """One decode step on a cached state: updates `h` in place, returns y (B, D).
+
+        h = exp(-dt*Aneg) * h + dt*B*x;   y = sum_n C*h
+
+    x, dt (B, D); B, C (B, N); Aneg (D, N); h (B, D, N), e.g. the state a
+    `return_state=True` scan returned. Not differentiable: it is the
+    inference path of the recurrent cache (reference model.py:228-241 runs
+    the same arithmetic as PyTorch ops). On CUDA tensors 'auto'/'cuda'/'metal'
+    run one fused kernel (mms_step); 'torch' runs selective_scan_step_ref and
+    copies the result into h. Off-CUDA, 'auto' returns None like
+    selective_scan.
+    """
+    if impl not in _IMPLS:
+        raise ValueError(f"unknown scan_impl {impl!r}; want 'auto', 'cuda', 'metal' or 'torch'")
+    if impl == "torch":
+        y, h_new = selective_scan_step_ref(x, dt, aneg, b_in, c_in, h)
+        h.copy_(h_new)
+        return y
+    if not x.is_cuda:
+        if impl in ("cuda", "metal"):
+            raise RuntimeError(f"scan_impl={impl!r} needs CUDA tensors (this build has no "
+                               f"MPS/Metal backend); got device {x.device.type!r}")
+        return None
+    if x.dim() != 2 or dt.shape != x.shape or aneg.dim() != 2:
+        raise ValueError(f"bad shapes: x {tuple(x.shape)}, dt {tuple(dt.shape)}, "
+                         f"Aneg {tuple(aneg.shape)}")
+    bt, d = x.shape
+    n = aneg.shape[1]
+    _validate(x.unsqueeze(1), dt.unsqueeze(1), aneg, b_in.unsqueeze(1), c_in.unsqueeze(1),
+              impl)
+    if h.shape != (bt, d, n) or h.dtype != torch.float32 or h.device != x.device:
+        raise ValueError(f"state h must be float32 ({bt}, {d}, {n}) on {x.device}; "
+                         f"got {h.dtype} {tuple(h.shape)} on {h.device}")
+    if not h.is_contiguous() or h.data_ptr() % 16:
+        raise ValueError("state h must be contiguous and 16-byte aligned (it is updated in place)")
+    if bt == 0 or d == 0:
+        return x.new_zeros(bt, d)
+    with torch.cuda.device(x.device):
+        return _native.step(_aligned(x, 4), _aligned(dt, 4), _aligned(aneg, 16),
+                            _aligned(b_in, 16), _aligned(c_in, 16), h)
