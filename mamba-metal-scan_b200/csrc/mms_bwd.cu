@@ -97,14 +97,14 @@ struct BwdShape {
 struct WorkCursor {
     int c, phase, sg, j;       // phase 0 = P, 1 = R, 2 = W; c < 0 when done
     int t0c, t1c, nseg, u0, u1, ngrp;
-    int T, K;
+    int T, K, clo;             // chunks clo .. (start) are this CTA's
 
-    __device__ void start(int T_, int K_) {
-        T = T_; K = K_;
-        enter_chunk((T + K - 1) / K - 1);
+    __device__ void start(int T_, int K_, int chi, int clo_) {
+        T = T_; K = K_; clo = clo_;
+        enter_chunk(chi);
     }
     __device__ void enter_chunk(int c_) {
-        c = c_;
+        c = c_ < clo ? -1 : c_;
         if (c < 0) return;
         t0c = c * K;
         t1c = min(t0c + K, T);
@@ -408,12 +408,27 @@ __device__ __forceinline__ void flush_group(const float *sd, int tid, int t0, in
     }
 }
 
+// Adjoint entering the CTA's last step: zero at the end of the sequence;
+// otherwise the carry the segment combine left for time segment `sg`, which is
+// the whole dA_{t+1} * g_{t+1} term (so the decay multiplying it is 1).
+template <int G>
+__device__ __forceinline__ void init_adjoint(Adjoint &A, const Lane<G> &L, const float *seg_e,
+                                             int sg, int nsg, int D, int N)
+{
+#pragma unroll
+    for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+    if (sg + 1 < nsg) {
+        L.load_state(A.gad, seg_e + ((size_t)L.b * nsg + sg) * D * N, N);
+        A.anx[0] = A.anx[1] = f2(1.f, 1.f);
+    }
+}
+
 template <int G>
 __device__ __forceinline__ void store_dacc(const Lane<G> &L, const Adjoint &A, float *part_a,
                                            int D, int N)
 {
     if (!L.act) return;
-    float *pa = part_a + ((size_t)L.b * D + L.d) * N + 4 * L.g;
+    float *pa = part_a + (((size_t)L.b * gridDim.z + blockIdx.z) * D + L.d) * N + 4 * L.g;
     pa[0 ^ L.tau] = -A.dac[0].x;
     pa[1 ^ L.tau] = -A.dac[0].y;
     pa[2 ^ L.tau] = -A.dac[1].x;
@@ -428,8 +443,8 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ Cm, const float *__restrict__ dy,
            const float *__restrict__ ckpt, float *__restrict__ dx,
            float *__restrict__ ddt, float *__restrict__ part_bc,
-           float *__restrict__ part_a, float *subck,
-           int T, int D, int N, int K, int nblk, int nsegk)
+           float *__restrict__ part_a, float *subck, const float *__restrict__ seg_e,
+           int T, int D, int N, int K, int nblk, int nsegk, int cps)
 {
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
@@ -449,8 +464,11 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
     float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
 
+    // time segment blockIdx.z: chunks [sg*cps, min((sg+1)*cps, nchunk))
+    const int sg = blockIdx.z, nsg = gridDim.z;
+    float *subb = subck + ((size_t)L.b * nsg + sg) * nsegk * plane;   // this CTA's slab
     WorkCursor cur, pre;
-    cur.start(T, K);
+    cur.start(T, K, min((sg + 1) * cps, nchunk) - 1, sg * cps);
     pre = cur;
 #pragma unroll
     for (int s = 0; s < NAT_BUFS; ++s) {
@@ -466,8 +484,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     rewrite_tile<G>(nat, der, tid);
 
     Adjoint A;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+    init_adjoint<G>(A, L, seg_e, sg, nsg, D, N);
     float2 hs[2];
     int cur_chunk = -1, cur_seg = -1;
     int nw = 0, pend_t0 = 0, pend_nv = 0;            // walked groups; the one awaiting its flush
@@ -508,7 +525,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             advance_tile<G>(hs, L.an2, v);
             if ((cur.j + 1) % SLOTS == 0 && L.act) {
                 const int q = (cur.j + 1) / SLOTS;
-                *reinterpret_cast<float4 *>(subck + ((size_t)L.b * nsegk + q) * plane + chan) =
+                *reinterpret_cast<float4 *>(subb + (size_t)q * plane + chan) =
                     make_float4(hs[0].x, hs[0].y, hs[1].x, hs[1].y);
             }
             continue;
@@ -519,7 +536,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
                 // written by this same thread in the pre-pass: coherent plain load
                 float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
                 if (L.act) w = *reinterpret_cast<const float4 *>(
-                    subck + ((size_t)L.b * nsegk + cur.sg) * plane + chan);
+                    subb + (size_t)cur.sg * plane + chan);
                 hs[0] = lo(w);
                 hs[1] = hi(w);
             } else if (cur.c > 0) {
@@ -570,7 +587,8 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ Cm, const float *__restrict__ dy,
               const float *__restrict__ ckpt, float *__restrict__ dx,
               float *__restrict__ ddt, float *__restrict__ part_bc,
-              float *__restrict__ part_a, int T, int D, int N, int nblk)
+              float *__restrict__ part_a, const float *__restrict__ seg_e,
+              int T, int D, int N, int nblk, int cps)
 {
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
@@ -611,9 +629,13 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         h[1] = f2(p[2 ^ L.tau], p[3 ^ L.tau]);
     };
 
+    // time segment blockIdx.z: groups chi .. clo, last to first
+    const int sg = blockIdx.z, nsg = gridDim.z;
+    const int clo = sg * cps, chi = min((sg + 1) * cps, nchunk) - 1;
+    const int ngrp = chi - clo + 1;
 #pragma unroll
     for (int s = 0; s < NAT_BUFS; ++s) {
-        if (nchunk - 1 - s >= 0) stage(s, nchunk - 1 - s);
+        if (chi - s >= clo) stage(s, chi - s);
         cp_commit();
     }
     cp_wait<NAT_BUFS - 1>();
@@ -623,23 +645,22 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     entry(hnext, 0);
 
     Adjoint A;
-#pragma unroll
-    for (int p = 0; p < 2; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+    init_adjoint<G>(A, L, seg_e, sg, nsg, D, N);
 
-    for (int it = 0; it < nchunk; ++it) {
-        const int c = nchunk - 1 - it;
+    for (int it = 0; it < ngrp; ++it) {
+        const int c = chi - it;
         cp_wait<NAT_BUFS - 2>();
         __syncthreads();
         if (it > 0)                                    // dB|dC of the group walked last
             flush_group<G>(sd + ((it - 1) & 1) * S::SDF, tid, (c + 1) * GRP,
                            min(GRP, T - (c + 1) * GRP), N, pbc);
         const float2 hb[2] = {hnext[0], hnext[1]};
-        if (c >= 1) {                                  // group it+1: rewrite, take its entry state
+        if (c - 1 >= clo) {                            // group it+1: rewrite, take its entry state
             const int nb = (it + 1) % NAT_BUFS;
             rewrite_tile<G>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid);
             entry(hnext, nb);
         }
-        if (c >= NAT_BUFS) stage((it + NAT_BUFS) % NAT_BUFS, c - NAT_BUFS);
+        if (c - NAT_BUFS >= clo) stage((it + NAT_BUFS) % NAT_BUFS, c - NAT_BUFS);
         cp_commit();
 
         const float *dtile = der + (it % DER_BUFS) * S::DERF;
@@ -653,7 +674,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     }
     cp_wait<0>();
     __syncthreads();
-    flush_group<G>(sd + ((nchunk - 1) & 1) * S::SDF, tid, 0, min(GRP, T), N, pbc);
+    flush_group<G>(sd + ((ngrp - 1) & 1) * S::SDF, tid, clo * GRP, min(GRP, T - clo * GRP), N, pbc);
     store_dacc<G>(L, A, part_a, D, N);
 }
 
@@ -676,14 +697,14 @@ __global__ void reduce_bc_kernel(const float *__restrict__ part, float *__restri
     }
 }
 
-// dAneg = sum over batch rows (fixed order).
+// dAneg = sum over the (batch row, time segment) partials (fixed order).
 __global__ void reduce_a_kernel(const float *__restrict__ part, float *__restrict__ daneg,
-                                int Bt, size_t DN)
+                                int rows, size_t DN)
 {
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < DN;
          idx += (size_t)gridDim.x * blockDim.x) {
         float s = 0.f;
-        for (int b = 0; b < Bt; ++b) s += part[(size_t)b * DN + idx];
+        for (int r = 0; r < rows; ++r) s += part[(size_t)r * DN + idx];
         daneg[idx] = s;
     }
 }
@@ -698,13 +719,21 @@ BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K)
     w.nblk = (D + dpb - 1) / dpb;
     const int kk = K < T ? K : T;
     w.nseg = (kk + SEG - 1) / SEG;
+    w.plan = seg_plan(Bt, T, D, N, K);
+    const size_t planes = (size_t)Bt * w.plan.S * D * N * sizeof(float);
     size_t off = 0;
     w.part_bc = off;
     off = align256(off + (size_t)Bt * w.nblk * T * 2 * N * sizeof(float));
     w.part_a = off;
-    off = align256(off + (size_t)Bt * D * N * sizeof(float));
+    off = align256(off + planes);
     w.subck = off;
-    if (w.nseg > 1) off = align256(off + (size_t)Bt * w.nseg * D * N * sizeof(float));
+    if (w.nseg > 1) off = align256(off + planes * w.nseg);
+    w.seg_e = w.seg_p = off;
+    if (w.plan.S > 1) {
+        off = align256(off + planes);
+        w.seg_p = off;
+        off = align256(off + planes);
+    }
     w.total = off;
     return w;
 }
@@ -718,21 +747,33 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     float *part_bc = reinterpret_cast<float *>(ws + w.part_bc);
     float *part_a = reinterpret_cast<float *>(ws + w.part_a);
     float *subck = reinterpret_cast<float *>(ws + w.subck);
-    dim3 grid(w.nblk, a.Bt);
+    float *seg_e = reinterpret_cast<float *>(ws + w.seg_e);
+    float *seg_p = reinterpret_cast<float *>(ws + w.seg_p);
+    const SegPlan sp = w.plan;
+    if (sp.S > 1) {
+        // local adjoint carries of segments 1..S-1, then the chain (last to first)
+        SegLocalArgs la{a.dy, a.dt, a.aneg, a.C, seg_e, seg_p, a.Bt, a.T, a.D, a.N,
+                        sp.cps * a.K, 1, sp.S - 1, sp.S, 1, 0, 0};
+        if ((e = launch_seg_local(la, true, stream)) != cudaSuccess) return e;
+        if ((e = launch_seg_combine_bwd(seg_e, seg_p, a.Bt, sp.S, (size_t)a.D * a.N, stream)) !=
+            cudaSuccess)
+            return e;
+    }
+    dim3 grid(w.nblk, a.Bt, sp.S);
     if (a.K == GRP) {
         e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM_K8);
         if (e != cudaSuccess) return e;
         bwd_kernel_k8<G, VEC><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
-            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a,
-            a.T, a.D, a.N, w.nblk);
+            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e,
+            a.T, a.D, a.N, w.nblk, sp.cps);
     } else {
         e = cudaFuncSetAttribute(bwd_kernel<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM);
         if (e != cudaSuccess) return e;
         bwd_kernel<G, VEC><<<grid, BWD_THREADS, S::SMEM, stream>>>(
-            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck,
-            a.T, a.D, a.N, a.K, w.nblk, w.nseg);
+            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck, seg_e,
+            a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t nbc = (size_t)a.Bt * a.T * 2 * a.N;
@@ -741,7 +782,7 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t dn = (size_t)a.D * a.N;
     const int ra = (int)((dn + 255) / 256 < 148 * 16 ? (dn + 255) / 256 : 148 * 16);
-    reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt, dn);
+    reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt * sp.S, dn);
     return cudaGetLastError();
 }
 

@@ -40,7 +40,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
 fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
            const float *__restrict__ Cm, float *__restrict__ y,
-           float *__restrict__ ckpt, int T, int D, int N, int K)
+           float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps)
 {
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
@@ -56,6 +56,10 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     const int b = blockIdx.y;
     const bool act = d < D && 4 * g < N;
     const int nchunk = (T + K - 1) / K;
+    // Time segment blockIdx.z of gridDim.z covers steps [tb, te) = chunks
+    // [sg*cps, (sg+1)*cps); a single segment is the whole sequence.
+    const int sg = blockIdx.z, nsg = gridDim.z;
+    const int tb = sg * L, te = min(T, tb + L);
 
     // -Aneg * log2(e) as two packed pairs: dA = 2^(dt * nan2).
     float2 nan2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
@@ -64,37 +68,47 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         nan2[0] = f2(-a4.x * MMS_LOG2E, -a4.y * MMS_LOG2E);
         nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
-    float2 h[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 
     const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
     float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N + 4 * g;
     float *yb = y + (size_t)b * T * D;
 
-    const int ntiles = (T + TT - 1) / TT;
+    // The state entering the segment: the checkpoint the segment combine left
+    // at the end of the previous segment (zero for the first).
+    float2 h[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+    if (sg > 0 && act) {
+        const float4 w = *reinterpret_cast<const float4 *>(ckb + (size_t)(sg * cps - 1) * D * N);
+        h[0] = lo(w);
+        h[1] = hi(w);
+    }
+    // that boundary checkpoint is final; the segment's own last one is left alone
+    const int ck_keep = sg + 1 < nsg ? (sg + 1) * cps - 1 : -1;
+
+    const int ntiles = (te - tb + TT - 1) / TT;
 #pragma unroll
     for (int s = 0; s < FWD_STAGES - 1; ++s) {
         if (s < ntiles)
             stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
-                                                              s * TT, min(TT, T - s * TT),
+                                                              tb + s * TT, min(TT, te - tb - s * TT),
                                                               d0, D, N, tid);
         cp_commit();
     }
 
-    int next_ck = min(K, T) - 1;                           // step whose state is checkpointed next
-    int chunk = 0;
+    int next_ck = min(tb + K, T) - 1;                      // step whose state is checkpointed next
+    int chunk = sg * cps;
     for (int k = 0; k < ntiles; ++k) {
         cp_wait<FWD_STAGES - 2>();
         __syncthreads();
         const int kn = k + FWD_STAGES - 1;
         if (kn < ntiles)
             stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(
-                tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, kn * TT, min(TT, T - kn * TT),
-                d0, D, N, tid);
+                tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, tb + kn * TT,
+                min(TT, te - tb - kn * TT), d0, D, N, tid);
         cp_commit();
 
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
-        const int t0 = k * TT;
+        const int t0 = tb + k * TT;
 #pragma unroll
         for (int j = 0; j < TT; ++j) {
             const float *row = tile + j * ROWF;
@@ -109,8 +123,9 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             h[1] = fma2(ex2x2(mul2(dt2, nan2[1])), h[1], mul2(bx2, hi(Bv)));
             const float2 acc = fma2(hi(Cv), h[1], mul2(lo(Cv), h[0]));
             ys[(j * DPB + c) * G + g] = acc.x + acc.y;
-            if (t0 + j == next_ck) {                       // uniform across the CTA
-                if (act) st4(ckb + (size_t)chunk * D * N, make_float4(h[0].x, h[0].y, h[1].x, h[1].y));
+            if (t0 + j == next_ck && t0 + j < te) {        // uniform across the CTA
+                if (act && chunk != ck_keep)
+                    st4(ckb + (size_t)chunk * D * N, make_float4(h[0].x, h[0].y, h[1].x, h[1].y));
                 ++chunk;
                 next_ck = min(next_ck + K, T - 1);
             }
@@ -131,7 +146,7 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 #pragma unroll
                 for (int q = 0; q < G; ++q) sum += src[q];
             }
-            if (t0 + j < T && d0 + cc < D) yb[(size_t)(t0 + j) * D + d0 + cc] = sum;
+            if (t0 + j < te && d0 + cc < D) yb[(size_t)(t0 + j) * D + d0 + cc] = sum;
         }
     }
 }
@@ -272,9 +287,21 @@ static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
     cudaError_t e = cudaFuncSetAttribute(fwd_kernel<G, VEC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt);
+    const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K);
+    const int nchunk = (a.T + a.K - 1) / a.K;
+    const int L = sp.cps * a.K;
+    if (sp.S > 1) {
+        // local end states and decay products of segments 0..S-2, then the chain
+        SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, L, 0,
+                        sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2};
+        if ((e = launch_seg_local(la, false, stream)) != cudaSuccess) return e;
+        if ((e = launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N,
+                                        stream)) != cudaSuccess)
+            return e;
+    }
+    dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt, sp.S);
     fwd_kernel<G, VEC><<<grid, FWD_THREADS, S::SMEM, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps);
     return cudaGetLastError();
 }
 

@@ -35,6 +35,40 @@ inline int groups_for(int N)
     return g;
 }
 
+// Time segments. A CTA of the G-lane kernels covers 256/G channels of one batch
+// row; when batch rows x channel blocks cannot fill the 148 SMs (long
+// sequences with few channels per GPU), the sequence is also cut into S
+// segments of `cps` checkpoint chunks (L = cps*K steps) that run in parallel.
+// A segment's entry state (forward) or adjoint carry (backward) comes from a
+// local pass over the other segments plus a sequential combine over S:
+//     state entering s+1 = P_s * (state entering s) + h_s
+// with h_s the segment's end state from a zero start and
+// P_s = prod over the segment of exp(-dt*Aneg) = exp(-Aneg * sum dt).
+// The forward and backward use the same plan (it depends on the shape only).
+constexpr int N_SM = 148;
+struct SegPlan {
+    int S;      // segments (1: no split)
+    int cps;    // checkpoint chunks per segment
+};
+
+inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
+{
+    const int dpb = 256 / groups_for(N);
+    const long long base = (long long)Bt * ((D + dpb - 1) / dpb);
+    const int nchunk = (T + K - 1) / K;
+    SegPlan p{1, nchunk};
+    if (base >= 2 * N_SM) return p;                 // a full wave without splitting
+    const long long want = (4LL * N_SM + base - 1) / base;
+    long long cps = (nchunk + want - 1) / want;
+    if (cps < 2) cps = 2;                           // the forward keeps P_s in chunk cps-2
+    if (cps * K < 64) cps = (64 + K - 1) / K;       // at least 64 steps per segment
+    const long long S = (nchunk + cps - 1) / cps;
+    if (S < 2) return p;
+    p.S = (int)S;
+    p.cps = (int)cps;
+    return p;
+}
+
 // 16-byte staging of (T, D) channel arrays is possible when every row starts
 // 16-byte aligned: D % 4 == 0 and 16-byte aligned base pointers.
 inline bool vec_ok(int D, const void *p0, const void *p1, const void *p2 = nullptr)
@@ -47,14 +81,34 @@ inline bool vec_ok(int D, const void *p0, const void *p1, const void *p2 = nullp
 // every region 256-byte aligned).
 struct BwdWorkspace {
     size_t part_bc;    // (Bt, nblk, T, 2N) per-CTA partial sums of dB|dC over its channels
-    size_t part_a;     // (Bt, D, N) per-batch-row partial sums of dAneg
-    size_t subck;      // (Bt, nseg, D, N) segment-start states inside long chunks
+    size_t part_a;     // (Bt*S, D, N) per-(batch row, time segment) partial sums of dAneg
+    size_t subck;      // (Bt*S, nseg, D, N) segment-start states inside long chunks
+    size_t seg_e;      // (Bt, S, D, N) adjoint carries of the time segments (S > 1)
+    size_t seg_p;      // (Bt, S, D, N) decay products of the time segments (S > 1)
     size_t total;
     int nblk;          // CTAs along D
     int nseg;          // segments per chunk (1 when K <= segment length)
+    SegPlan plan;      // time segments
 };
 
 BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K);
+
+// Segment passes (mms_seg.cu). `u` is x (forward) or dy (backward), `row` is
+// B (forward) or C (backward); segments s_first .. s_first+nseg-1 are scanned
+// from a zero start and their end value / decay product stored at
+// (b*bplanes + s*splanes + off) * D*N in vout / pout.
+struct SegLocalArgs {
+    const float *u, *dt, *aneg, *row;
+    float *vout, *pout;
+    int Bt, T, D, N, L, s_first, nseg, bplanes, splanes, voff, poff;
+};
+cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream);
+// forward: chain the segment end states through the checkpoint slots
+cudaError_t launch_seg_combine_fwd(float *ckpt, int Bt, int nchunk, int S, int cps, size_t DN,
+                                   cudaStream_t stream);
+// backward: chain the adjoint carries in place; afterwards E[b, s] is the carry into segment s
+cudaError_t launch_seg_combine_bwd(float *E, const float *P, int Bt, int S, size_t DN,
+                                   cudaStream_t stream);
 
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream);
 cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream);

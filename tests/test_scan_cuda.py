@@ -101,6 +101,36 @@ def test_wide_channel_counts_match_the_float64_oracle(bt, t_len, d, n, chunk):
     assert max_rel(ckpt, ckpt64) <= FWD_TOL
 
 
+# Long sequences with few channels: the kernels cut the sequence into time
+# segments that run in parallel and chain their entry states and adjoint
+# carries (csrc/mms_seg.cu). `slow` shrinks dt 50x so states and adjoints
+# survive across many segments and a wrong carry cannot hide behind decay.
+LONG = [(1, 4096, 256, 16, 8, False), (1, 4096, 256, 16, 8, True), (1, 3001, 130, 12, 8, True),
+        (2, 2000, 64, 64, 8, True), (1, 5000, 96, 16, 64, True), (1, 1234, 40, 8, 7, True),
+        (1, 4096, 64, 4, 100, True), (3, 700, 16, 16, 8, True)]
+
+
+@pytest.mark.parametrize("bt,t_len,d,n,chunk,slow", LONG)
+def test_long_sequences_match_the_float64_oracle(bt, t_len, d, n, chunk, slow):
+    x, dt, aneg, b_in, c_in, dy = inputs(bt, t_len, d, n, "c0", seed=t_len + d, device=DEV)
+    if slow:
+        dt = dt * 0.02
+    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    y64, ckpt64, g64 = oracle64(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)} chunk {chunk} slow {slow}")
+    from mamba_metal import _native
+    _, ckpt = _native.fwd(x, dt, aneg, b_in, c_in, chunk)
+    assert max_rel(ckpt, ckpt64) <= FWD_TOL
+
+
+def test_config3_shape_matches_the_float64_oracle():
+    """One sequence of config 3 per GPU: B=1, T=16384, d_inner=2048, d_state=16."""
+    x, dt, aneg, b_in, c_in, dy = inputs(1, 16384, 2048, 16, "c0", seed=3, device=DEV)
+    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=8)
+    y64, _, g64 = oracle64(x, dt, aneg, b_in, c_in, dy, chunk=8)
+    assert_parity(y, grads, y64, g64, "config 3")
+
+
 @pytest.mark.parametrize("path", sorted(GOLDEN.glob("*.npz")), ids=lambda p: p.stem)
 def test_golden_vectors_from_the_reference(path):
     """The reference's own outputs (fp32 and fp64), recorded by tests/golden/make_golden.py."""
