@@ -153,48 +153,59 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 
 
 // ---------------------------------------------------------------------------
-// Whole-state variant for 8 < N <= 16: one thread per (b, d) channel holds all
-// 16 states. y_t is then a sum inside the thread (no cross-lane reduction, no
-// shared-memory round trip, one coalesced store per step), B_t and C_t are
-// warp-wide broadcast loads, and each step offers 16 independent ex2 to keep
-// the MUFU queue full. Used when there are enough channels to fill the GPU
-// (B*D >= S16_MIN_CHANNELS); otherwise the G-lane kernel above gives more
+// Whole-state variant for 8 < N <= 16: LPC (1 or 2) threads per (b, d)
+// channel hold its 16 states, 16/LPC each. y_t is then a sum inside the thread
+// (plus one shuffle for LPC = 2): no shared-memory round trip, one coalesced
+// store per step; B_t and C_t are broadcast loads, and each step offers 16/LPC
+// independent ex2 per thread. Used when there are enough channels to fill the
+// GPU (B*D >= S16_MIN_CHANNELS); otherwise the G-lane kernel above gives more
 // threads.
-constexpr int S16_THREADS = 128;
+#ifndef MMS_FWD_LPC
+#define MMS_FWD_LPC 1
+#endif
+constexpr int S16_DPB = 128;                                 // channels per CTA
 constexpr int S16_TT = 16;
-constexpr int S16_MIN_CHANNELS = 148 * S16_THREADS;
+constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
+template <int LPC>
 struct S16Shape {
-    static constexpr int DPB = S16_THREADS;                  // channels per CTA
+    static constexpr int THREADS = S16_DPB * LPC;
+    static constexpr int DPB = S16_DPB;
+    static constexpr int SPT = 16 / LPC;                     // states per thread
     static constexpr int ROWF = 2 * DPB + 2 * 16;            // x, dt, B, C floats per step
     static constexpr size_t SMEM = sizeof(float) * (size_t)FWD_STAGES * S16_TT * ROWF;
 };
 
-template <bool VEC>
-__global__ void __launch_bounds__(S16_THREADS, 2)
+template <int LPC, bool VEC>
+__global__ void __launch_bounds__(S16Shape<LPC>::THREADS, LPC == 1 ? 2 : 3)
 fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, float *__restrict__ y,
                float *__restrict__ ckpt, int T, int D, int N, int K)
 {
-    constexpr int DPB = S16Shape::DPB, ROWF = S16Shape::ROWF, TT = S16_TT;
+    using S = S16Shape<LPC>;
+    constexpr int DPB = S::DPB, ROWF = S::ROWF, TT = S16_TT, SPT = S::SPT, NP = SPT / 2;
+    constexpr int THREADS = S::THREADS;
     extern __shared__ __align__(16) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
 
     const int tid = threadIdx.x;
+    const int c = tid / LPC;                               // channel within the CTA
+    const int l = tid % LPC;                               // states [l*SPT, (l+1)*SPT)
     const int d0 = blockIdx.x * DPB;
-    const int d = d0 + tid;
+    const int d = d0 + c;
     const int b = blockIdx.y;
     const bool dval = d < D;
     const int nchunk = (T + K - 1) / K;
+    const int n0 = l * SPT;
 
-    // -Aneg * log2(e) for the 16 states (zero past N): dA = 2^(dt * nan2).
-    float2 nan2[8], h[8];
+    // -Aneg * log2(e) for this thread's states (zero past N): dA = 2^(dt * nan2).
+    float2 nan2[NP], h[NP];
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
+    for (int p = 0; p < NP; ++p) {
         float a0 = 0.f, a1 = 0.f;
-        if (dval && 2 * p < N) {
-            const float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + 2 * p);
+        if (dval && n0 + 2 * p < N) {
+            const float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + n0 + 2 * p);
             a0 = -v.x * MMS_LOG2E;
             a1 = -v.y * MMS_LOG2E;
         }
@@ -204,16 +215,16 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
 
     const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
-    float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N;
+    float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N + n0;
     float *yb = y + (size_t)b * T * D + d;
 
     const int ntiles = (T + TT - 1) / TT;
 #pragma unroll
     for (int s = 0; s < FWD_STAGES - 1; ++s) {
         if (s < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, S16_THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb,
-                                                            Bb, Cb, s * TT, min(TT, T - s * TT),
-                                                            d0, D, N, tid);
+            stage_tile<2, 2, DPB, 16, TT, THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb,
+                                                        Bb, Cb, s * TT, min(TT, T - s * TT),
+                                                        d0, D, N, tid);
         cp_commit();
     }
 
@@ -224,7 +235,7 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         __syncthreads();
         const int kn = k + FWD_STAGES - 1;
         if (kn < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, S16_THREADS, VEC>(
+            stage_tile<2, 2, DPB, 16, TT, THREADS, VEC>(
                 tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, kn * TT,
                 min(TT, T - kn * TT), d0, D, N, tid);
         cp_commit();
@@ -235,28 +246,30 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         for (int j = 0; j < TT; ++j) {
             const float *row = tile + j * ROWF;
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = row[tid];
-            const float dtv = row[DPB + tid];
-            const float4 *bc = reinterpret_cast<const float4 *>(row + 2 * DPB);
+            const float xv = row[c];
+            const float dtv = row[DPB + c];
+            const float4 *bc = reinterpret_cast<const float4 *>(row + 2 * DPB + n0);
             const float bx = dtv * xv;
             const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
             float2 acc = f2(0.f, 0.f);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < SPT / 4; ++q) {
                 const float4 Bv = bc[q], Cv = bc[4 + q];
                 h[2 * q] = fma2(ex2x2(mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
                 h[2 * q + 1] = fma2(ex2x2(mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1], mul2(bx2, hi(Bv)));
                 acc = fma2(lo(Cv), h[2 * q], acc);
                 acc = fma2(hi(Cv), h[2 * q + 1], acc);
             }
+            float yv = acc.x + acc.y;
+            if constexpr (LPC == 2) yv += __shfl_xor_sync(0xffffffffu, yv, 1);
             const int t = t0 + j;
-            if (dval && t < T) yb[(size_t)t * D] = acc.x + acc.y;
+            if (dval && l == 0 && t < T) yb[(size_t)t * D] = yv;
             if (t == next_ck) {                            // uniform across the CTA
                 if (dval) {
                     float *o = ckb + (size_t)chunk * D * N;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (4 * q < N)
+                    for (int q = 0; q < SPT / 4; ++q)
+                        if (n0 + 4 * q < N)
                             st4(o + 4 * q, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x,
                                                        h[2 * q + 1].y));
                 }
@@ -270,12 +283,13 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
 template <bool VEC>
 static cudaError_t launch_fwd_s16(const FwdArgs &a, cudaStream_t stream)
 {
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)S16Shape::SMEM);
+    constexpr int LPC = MMS_FWD_LPC;
+    using S = S16Shape<LPC>;
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<LPC, VEC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt);
-    fwd_kernel_s16<VEC><<<grid, S16_THREADS, S16Shape::SMEM, stream>>>(
+    dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt);
+    fwd_kernel_s16<LPC, VEC><<<grid, S::THREADS, S::SMEM, stream>>>(
         a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
     return cudaGetLastError();
 }

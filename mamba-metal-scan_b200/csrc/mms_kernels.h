@@ -57,7 +57,9 @@ inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
     const long long base = (long long)Bt * ((D + dpb - 1) / dpb);
     const int nchunk = (T + K - 1) / K;
     SegPlan p{1, nchunk};
-    if (base >= 2 * N_SM) return p;                 // a full wave without splitting
+    // Splitting costs a local pass over S-1 segments (about 40 % more work for
+    // a fwd+bwd step), which pays only below one CTA per SM.
+    if (base >= N_SM) return p;
     const long long want = (4LL * N_SM + base - 1) / base;
     long long cps = (nchunk + want - 1) / want;
     if (cps < 2) cps = 2;                           // the forward keeps P_s in chunk cps-2
