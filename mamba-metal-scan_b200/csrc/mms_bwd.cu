@@ -58,11 +58,6 @@ namespace mms {
 #ifndef MMS_BWD_MINB
 #define MMS_BWD_MINB 2
 #endif
-// Decays of a rebuilt group for its walk: 0 recomputes them (MUFU), 1 keeps
-// them in registers, 2 keeps them in shared memory.
-#ifndef MMS_WALK_KEEP_A
-#define MMS_WALK_KEEP_A 0
-#endif
 #ifndef MMS_BWD_K8_MINB
 #define MMS_BWD_K8_MINB 2
 #endif
@@ -90,9 +85,8 @@ struct BwdShape {
     static constexpr size_t SLOTF = (size_t)SLOTS * BWD_THREADS * 4;
     static constexpr size_t SDF = (size_t)GRP * BWD_WARPS * NV2;   // one of two buffers
     static constexpr size_t CKF = (size_t)DPB * NPAD;            // entry-state slab of a group
-    static constexpr size_t STASHF = MMS_WALK_KEEP_A == 2 ? (size_t)GRP * BWD_THREADS * 4 : 0;
     static constexpr size_t SMEM_K8 =
-        sizeof(float) * ((size_t)NAT_BUFS * (NATF + CKF) + (size_t)DER_BUFS * DERF + 2 * SDF + STASHF);
+        sizeof(float) * ((size_t)NAT_BUFS * (NATF + CKF) + (size_t)DER_BUFS * DERF + 2 * SDF);
     static constexpr size_t SMEM = SMEM_K8 + sizeof(float) * SLOTF;
 };
 
@@ -277,19 +271,21 @@ struct Adjoint {
 // Rebuild one group from the state entering it, then walk it backwards:
 // dx/ddt are finished with shuffles across the channel's lanes and stored
 // (dxo/ddto point at this lane's channel at step t0), per-warp dB/dC sums go to sd.
+#ifndef MMS_WALK_KEEP_A
+#define MMS_WALK_KEEP_A 0
+#endif
 
 template <int G, bool FULL>
 __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&hb)[2],
                                            const Lane<G> &L, Adjoint &A, int nv,
-                                           float *dxo, float *ddto, int D, float *sd,
-                                           float4 *stash)
+                                           float *dxo, float *ddto, int D, float *sd)
 {
     float *outp = L.n_ddt ? ddto : dxo;
     using S = BwdShape<G>;
     constexpr int NPAD = S::NPAD, NV2 = S::NV2;
     // Rebuild: the states of the group's steps (and, when kept, their decays).
     float2 hv[GRP][2];
-#if MMS_WALK_KEEP_A == 1
+#if MMS_WALK_KEEP_A
     float2 av[GRP][2];
 #endif
 #pragma unroll
@@ -303,11 +299,9 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
             const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
             const float2 a0 = ex2x2(mul2(md, L.an2[0]));
             const float2 a1 = ex2x2(mul2(md, L.an2[1]));
-#if MMS_WALK_KEEP_A == 1
+#if MMS_WALK_KEEP_A
             av[i][0] = a0;
             av[i][1] = a1;
-#elif MMS_WALK_KEEP_A == 2
-            stash[i * BWD_THREADS] = make_float4(a0.x, a0.y, a1.x, a1.y);
 #endif
             hv[i][0] = fma2(a0, i ? hv[i > 0 ? i - 1 : 0][0] : hb[0], mul2(bx2, lo(Bv)));
             hv[i][1] = fma2(a1, i ? hv[i > 0 ? i - 1 : 0][1] : hb[1], mul2(bx2, hi(Bv)));
@@ -327,18 +321,14 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
             const float2 dy2 = f2(dyv, dyv), dt2 = f2(dtv, dtv);
             const float dxv = dtv * xv;
             const float2 dxv2 = f2(dxv, dxv);
-#if MMS_WALK_KEEP_A == 0
+#if !MMS_WALK_KEEP_A
             const float2 md = f2(-dtv, -dtv);
-#elif MMS_WALK_KEEP_A == 2
-            const float4 aw = stash[i * BWD_THREADS];
 #endif
             float2 p1 = f2(0.f, 0.f), p2 = f2(0.f, 0.f), vb[2], vc[2];
 #pragma unroll
             for (int p = 0; p < 2; ++p) {
-#if MMS_WALK_KEEP_A == 1
+#if MMS_WALK_KEEP_A
                 const float2 ai = av[i][p];
-#elif MMS_WALK_KEEP_A == 2
-                const float2 ai = p ? hi(aw) : lo(aw);
 #else
                 const float2 am = mul2(md, L.an2[p]);
                 const float2 ai = f2(ex2_fresh(am.x), ex2_fresh(am.y));
@@ -463,7 +453,6 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     float *der = nat + NAT_BUFS * S::NATF;                           // [DER_BUFS][DERF]
     float *sd = der + DER_BUFS * S::DERF;                            // [2][GRP][WARPS][NV2]
     float4 *slots = reinterpret_cast<float4 *>(sd + 2 * S::SDF);     // [SLOTS][THREADS]
-    float4 *stash = slots + SLOTS * BWD_THREADS + threadIdx.x;         // [GRP][THREADS] if kept
 
     const Lane<G> L(aneg, D, N);
     const int tid = L.tid;
@@ -576,8 +565,8 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         }
         float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
         float *sdb = sd + (nw & 1) * S::SDF;
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb, stash);
-        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb, stash);
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
         ++nw;
         pend_t0 = t0;
         pend_nv = nv;
@@ -608,7 +597,6 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     float *der = nat + NAT_BUFS * S::NATF;
     float *sd = der + DER_BUFS * S::DERF;               // [2][GRP][WARPS][NV2]
     float *cks = sd + 2 * S::SDF;                      // [NAT_BUFS][DPB][NPAD] entry states
-    float4 *stash = reinterpret_cast<float4 *>(cks + NAT_BUFS * S::CKF) + threadIdx.x;
 
     const Lane<G> L(aneg, D, N);
     const int tid = L.tid;
@@ -681,8 +669,8 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const int nv = min(GRP, T - t0);
         float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
         float *sdb = sd + (it & 1) * S::SDF;
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb, stash);
-        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb, stash);
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
     }
     cp_wait<0>();
     __syncthreads();
