@@ -153,59 +153,61 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 
 
 // ---------------------------------------------------------------------------
-// Whole-state variant for 8 < N <= 16: LPC (1 or 2) threads per (b, d)
-// channel hold its 16 states, 16/LPC each. y_t is then a sum inside the thread
-// (plus one shuffle for LPC = 2): no shared-memory round trip, one coalesced
-// store per step; B_t and C_t are broadcast loads, and each step offers 16/LPC
-// independent ex2 per thread. Used when there are enough channels to fill the
-// GPU (B*D >= S16_MIN_CHANNELS); otherwise the G-lane kernel above gives more
-// threads.
-#ifndef MMS_FWD_LPC
-#define MMS_FWD_LPC 1
-#endif
-constexpr int S16_DPB = 128;                                 // channels per CTA
+// Whole-state variant for 8 < N <= 16: one thread per (b, d) channel holds all
+// 16 states. y_t is then a sum inside the thread (no cross-lane reduction),
+// B_t and C_t are broadcast loads, and each step offers 16 independent ex2.
+// Used when there are enough channels to fill the GPU (B*D >= S16_MIN_CHANNELS);
+// otherwise the G-lane kernel above gives more threads.
+//
+// Output (BULK): y rows and checkpoints are written to shared memory and
+// leave for HBM on the bulk-copy engine, one tile later, so the 226 MB of y +
+// checkpoint writes at config 1 do not occupy the warps' load/store issue.
+// Per tile of 16 steps: y rows [16][128] and up to two checkpoint slabs of
+// 128 channels x N (each a contiguous block of ckpt), double buffered; a
+// third checkpoint in one tile (only the t = T-1 one can be) is stored
+// directly.
+constexpr int S16_DPB = 128;                                 // channels (= threads) per CTA
 constexpr int S16_TT = 16;
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
-template <int LPC>
 struct S16Shape {
-    static constexpr int THREADS = S16_DPB * LPC;
     static constexpr int DPB = S16_DPB;
-    static constexpr int SPT = 16 / LPC;                     // states per thread
     static constexpr int ROWF = 2 * DPB + 2 * 16;            // x, dt, B, C floats per step
-    static constexpr size_t SMEM = sizeof(float) * (size_t)FWD_STAGES * S16_TT * ROWF;
+    static constexpr size_t TILEF = (size_t)FWD_STAGES * S16_TT * ROWF;
+    static constexpr size_t YF = (size_t)2 * S16_TT * DPB;   // [2][TT][DPB]
+    static constexpr size_t CKF = (size_t)2 * 2 * DPB * 16;  // [2][2][DPB*N]
+    static constexpr size_t SMEM = sizeof(float) * TILEF;
+    static constexpr size_t SMEM_BULK = sizeof(float) * (TILEF + YF + CKF);
 };
 
-template <int LPC, bool VEC>
-__global__ void __launch_bounds__(S16Shape<LPC>::THREADS, LPC == 1 ? 2 : 3)
+template <bool VEC, bool BULK>
+__global__ void __launch_bounds__(S16_DPB, 2)
 fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, float *__restrict__ y,
                float *__restrict__ ckpt, int T, int D, int N, int K)
 {
-    using S = S16Shape<LPC>;
-    constexpr int DPB = S::DPB, ROWF = S::ROWF, TT = S16_TT, SPT = S::SPT, NP = SPT / 2;
-    constexpr int THREADS = S::THREADS;
+    constexpr int DPB = S16Shape::DPB, ROWF = S16Shape::ROWF, TT = S16_TT;
     extern __shared__ __align__(16) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
+    float *ys = smem + S16Shape::TILEF;                    // BULK: [2][TT][DPB]
+    float *cks = ys + S16Shape::YF;                        // BULK: [2][2][DPB*N]
 
     const int tid = threadIdx.x;
-    const int c = tid / LPC;                               // channel within the CTA
-    const int l = tid % LPC;                               // states [l*SPT, (l+1)*SPT)
     const int d0 = blockIdx.x * DPB;
-    const int d = d0 + c;
+    const int d = d0 + tid;
     const int b = blockIdx.y;
     const bool dval = d < D;
+    const int dcnt = min(DPB, D - d0);
     const int nchunk = (T + K - 1) / K;
-    const int n0 = l * SPT;
 
-    // -Aneg * log2(e) for this thread's states (zero past N): dA = 2^(dt * nan2).
-    float2 nan2[NP], h[NP];
+    // -Aneg * log2(e) for the 16 states (zero past N): dA = 2^(dt * nan2).
+    float2 nan2[8], h[8];
 #pragma unroll
-    for (int p = 0; p < NP; ++p) {
+    for (int p = 0; p < 8; ++p) {
         float a0 = 0.f, a1 = 0.f;
-        if (dval && n0 + 2 * p < N) {
-            const float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + n0 + 2 * p);
+        if (dval && 2 * p < N) {
+            const float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + 2 * p);
             a0 = -v.x * MMS_LOG2E;
             a1 = -v.y * MMS_LOG2E;
         }
@@ -215,61 +217,87 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
 
     const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
-    float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N + n0;
+    float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N;
     float *yb = y + (size_t)b * T * D + d;
+
+    // BULK: send tile kp's y rows and its (up to two) checkpoint slabs.
+    auto send = [&](int kp, int nck, int ck0, int ck1) {
+        const int t0p = kp * TT, rows = min(TT, T - t0p);
+        const float *ysrc = ys + (kp & 1) * TT * DPB;
+        for (int r = 0; r < rows; ++r)
+            bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB, dcnt * 4u);
+        for (int i = 0; i < nck; ++i)
+            bulk_store(ckpt + ((size_t)b * nchunk + (i ? ck1 : ck0)) * D * N + (size_t)d0 * N,
+                       cks + ((kp & 1) * 2 + i) * DPB * N, (uint32_t)dcnt * N * 4u);
+        bulk_commit();
+    };
 
     const int ntiles = (T + TT - 1) / TT;
 #pragma unroll
     for (int s = 0; s < FWD_STAGES - 1; ++s) {
         if (s < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb,
-                                                        Bb, Cb, s * TT, min(TT, T - s * TT),
-                                                        d0, D, N, tid);
+            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
+                                                    s * TT, min(TT, T - s * TT), d0, D, N, tid);
         cp_commit();
     }
 
     int next_ck = min(K, T) - 1;
     int chunk = 0;
+    int nck = 0, ck0 = 0, ck1 = 0;                         // checkpoints of the current tile
+    int pnck = 0, pck0 = 0, pck1 = 0;                      // ... of the previous tile
     for (int k = 0; k < ntiles; ++k) {
+        if constexpr (BULK) {
+            if (k > 0) fence_async_smem();                 // tile k-1's y / checkpoints
+            if (tid == 0) bulk_wait_read<0>();             // tile k-2's copies have left set k&1
+        }
         cp_wait<FWD_STAGES - 2>();
         __syncthreads();
+        if constexpr (BULK) {
+            if (k > 0 && tid == 0) send(k - 1, pnck, pck0, pck1);
+        }
         const int kn = k + FWD_STAGES - 1;
         if (kn < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, THREADS, VEC>(
+            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(
                 tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, kn * TT,
                 min(TT, T - kn * TT), d0, D, N, tid);
         cp_commit();
 
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
+        float *yrow = ys + (k & 1) * TT * DPB + tid;
         const int t0 = k * TT;
+        nck = 0;
 #pragma unroll 4
         for (int j = 0; j < TT; ++j) {
             const float *row = tile + j * ROWF;
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = row[c];
-            const float dtv = row[DPB + c];
-            const float4 *bc = reinterpret_cast<const float4 *>(row + 2 * DPB + n0);
+            const float xv = row[tid];
+            const float dtv = row[DPB + tid];
+            const float4 *bc = reinterpret_cast<const float4 *>(row + 2 * DPB);
             const float bx = dtv * xv;
             const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
             float2 acc = f2(0.f, 0.f);
 #pragma unroll
-            for (int q = 0; q < SPT / 4; ++q) {
+            for (int q = 0; q < 4; ++q) {
                 const float4 Bv = bc[q], Cv = bc[4 + q];
                 h[2 * q] = fma2(ex2x2(mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
                 h[2 * q + 1] = fma2(ex2x2(mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1], mul2(bx2, hi(Bv)));
                 acc = fma2(lo(Cv), h[2 * q], acc);
                 acc = fma2(hi(Cv), h[2 * q + 1], acc);
             }
-            float yv = acc.x + acc.y;
-            if constexpr (LPC == 2) yv += __shfl_xor_sync(0xffffffffu, yv, 1);
             const int t = t0 + j;
-            if (dval && l == 0 && t < T) yb[(size_t)t * D] = yv;
+            if constexpr (BULK) yrow[j * DPB] = acc.x + acc.y;
+            else if (dval && t < T) yb[(size_t)t * D] = acc.x + acc.y;
             if (t == next_ck) {                            // uniform across the CTA
+                float *o = ckb + (size_t)chunk * D * N;
+                if (BULK && nck < 2) {
+                    o = cks + ((k & 1) * 2 + nck) * DPB * N + tid * N;
+                    if (nck == 0) ck0 = chunk; else ck1 = chunk;
+                    ++nck;
+                }
                 if (dval) {
-                    float *o = ckb + (size_t)chunk * D * N;
 #pragma unroll
-                    for (int q = 0; q < SPT / 4; ++q)
-                        if (n0 + 4 * q < N)
+                    for (int q = 0; q < 4; ++q)
+                        if (4 * q < N)
                             st4(o + 4 * q, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x,
                                                        h[2 * q + 1].y));
                 }
@@ -277,21 +305,44 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                 next_ck = min(next_ck + K, T - 1);
             }
         }
+        pnck = nck;
+        pck0 = ck0;
+        pck1 = ck1;
+    }
+    if constexpr (BULK) {
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            send(ntiles - 1, pnck, pck0, pck1);
+            bulk_wait<0>();
+        }
     }
 }
 
-template <bool VEC>
-static cudaError_t launch_fwd_s16(const FwdArgs &a, cudaStream_t stream)
+template <bool VEC, bool BULK>
+static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, cudaStream_t stream)
 {
-    constexpr int LPC = MMS_FWD_LPC;
-    using S = S16Shape<LPC>;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<LPC, VEC>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    const size_t smem = BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt);
-    fwd_kernel_s16<LPC, VEC><<<grid, S::THREADS, S::SMEM, stream>>>(
+    dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt);
+    fwd_kernel_s16<VEC, BULK><<<grid, S16_DPB, smem, stream>>>(
         a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
     return cudaGetLastError();
+}
+
+#ifndef MMS_FWD_BULK
+#define MMS_FWD_BULK 1
+#endif
+
+static cudaError_t launch_fwd_s16(const FwdArgs &a, cudaStream_t stream)
+{
+    // The bulk path needs 16-byte aligned y rows (D % 4 == 0, aligned y) and
+    // suits strides K >= 8 (at most two checkpoints per 16-step tile).
+    if (!vec_ok(a.D, a.x, a.dt)) return launch_fwd_s16_vb<false, false>(a, stream);
+    if (MMS_FWD_BULK && a.K >= 8 && vec_ok(a.D, a.y, a.y)) return launch_fwd_s16_vb<true, true>(a, stream);
+    return launch_fwd_s16_vb<true, false>(a, stream);
 }
 
 template <int G, bool VEC>
@@ -329,8 +380,7 @@ static cudaError_t launch_fwd_g(const FwdArgs &a, cudaStream_t stream)
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)
 {
     if (groups_for(a.N) == 4 && (long long)a.Bt * a.D >= S16_MIN_CHANNELS)
-        return vec_ok(a.D, a.x, a.dt) ? launch_fwd_s16<true>(a, stream)
-                                      : launch_fwd_s16<false>(a, stream);
+        return launch_fwd_s16(a, stream);
     switch (groups_for(a.N)) {
     case 1: return launch_fwd_g<1>(a, stream);
     case 2: return launch_fwd_g<2>(a, stream);

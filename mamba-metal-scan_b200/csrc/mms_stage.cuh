@@ -30,6 +30,27 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 template <int N>
 __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
 
+// Asynchronous shared -> global copy on the bulk-copy (TMA) engine, no tensor
+// map: both addresses 16-byte aligned, bytes a multiple of 16. The issuing
+// thread continues at once; smem written by ordinary stores must be published
+// to the async proxy first (fence_async_smem by the writers, then a barrier).
+__device__ __forceinline__ void bulk_store(void *gdst, const void *ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n"
+                 ::"l"(gdst), "r"(smem_u32(ssrc)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// Wait until at most N committed groups are still reading their smem sources.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(N) : "memory");
+}
+// Wait until at most N committed groups are incomplete.
+template <int N>
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group %0;\n" ::"n"(N) : "memory"); }
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
 // Copy `rows` consecutive time steps [t0, t0+rows) of NARR channel arrays
 // (each (T, D) row-major, already offset to the batch row) and of NBC state
 // arrays (each (T, N)) into a tile laid out per step as
