@@ -58,6 +58,9 @@ namespace mms {
 #ifndef MMS_BWD_MINB
 #define MMS_BWD_MINB 2
 #endif
+#ifndef MMS_BWD_W8
+#define MMS_BWD_W8 1
+#endif
 #ifndef MMS_BWD_K8_MINB
 #define MMS_BWD_K8_MINB 2
 #endif
@@ -760,7 +763,9 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
-    if (a.K == GRP) {
+    if (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K)) {
+        e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
+    } else if (a.K == GRP) {
         e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM_K8);
         if (e != cudaSuccess) return e;

@@ -1,0 +1,379 @@
+// Backward selective scan, 8 states per lane (8 < N <= 16, checkpoint stride 8).
+//
+// Same mathematics as mms_bwd.cu (reference mamba_metal/scan.py:26-34, kernel
+// ssm_bwd at :132-261); a different decomposition for the d_state 12/16 case:
+// two lanes share a channel and each holds 8 of its 16 states. Compared with
+// four lanes of 4 states, every per-step cost that does not depend on the
+// state count (x/dt/dy loads and products, the dx/ddt sum over the channel's
+// lanes, loop and address work) is spread over 8 states instead of 4, and
+// the dx/ddt sum needs one shuffle level instead of two.
+//
+// A CTA of 128 threads covers 64 channels of one batch row and walks its
+// checkpoint chunks (8 steps each) last to first. Per chunk:
+//   * the chunk's inputs and its entry checkpoint arrive by cp.async two
+//     chunks ahead; after a barrier they are rewritten once into the layouts
+//     the walk reads (x, dt, dy as 4-step runs per channel; B and C in the 8
+//     lane-specific state orders below); a second barrier publishes them;
+//   * the chunk is walked as two 4-step groups, later one first. A group's
+//     states are rebuilt from the state entering it and kept in registers
+//     (4 steps x 8 states). The later group starts 4 steps into the chunk, so
+//     the first 4 steps are advanced once more to reach it (1.5 rebuilds per
+//     step instead of 1 in exchange for half the registers).
+// Reductions (deterministic, no atomics):
+//   * dx, ddt: the two lanes of a channel exchange one value (transposed
+//     pair); the lane with the first half stores dx, the other ddt;
+//   * dB, dC over the warp's 16 channels: a transposed butterfly over lane
+//     bits 4, 3, 2 (where the lane's state order r XOR tau, tau = lane bits
+//     2..4, makes every level select-free) and a last transposed level over
+//     lane bit 1 (dB vs dC). Each lane ends with one value; the CTA's four
+//     warps are summed per step into one partial per CTA (reduce_bc_kernel
+//     adds the CTAs);
+//   * dAneg: register sums over the walk, one partial per (batch row, time
+//     segment).
+#include "mms_common.cuh"
+#include "mms_kernels.h"
+#include "mms_stage.cuh"
+
+namespace mms {
+
+namespace {
+
+constexpr int W8_THREADS = 128;
+constexpr int W8_WARPS = W8_THREADS / 32;
+constexpr int W8_DPB = W8_THREADS / 2;          // channels per CTA
+constexpr int W8_CH = 8;                        // steps per chunk (the checkpoint stride)
+constexpr int W8_NAT = 3;                       // natural-layout stages
+constexpr float W8_LN2 = 0.6931471805599453f;
+
+struct W8Shape {
+    static constexpr int NROWF = 3 * W8_DPB + 2 * 16;          // x, dt, dy, B, C per step
+    static constexpr int NATF = W8_CH * NROWF;
+    static constexpr int CKF = W8_DPB * 16;                    // entry-state slab
+    static constexpr int STAGEF = NATF + CKF;
+    static constexpr int QF = W8_CH * W8_DPB;                  // one array as 4-step runs
+    static constexpr int PF = W8_CH * 8 * 16;                  // B or C in 8 state orders
+    static constexpr int DERF = 3 * QF + 2 * PF;
+    static constexpr int SDF = W8_CH * W8_WARPS * 32;          // per-warp dB|dC sums
+    static constexpr size_t SMEM = sizeof(float) * ((size_t)W8_NAT * STAGEF + DERF + SDF);
+};
+
+__device__ __forceinline__ float2 shfl2x(float2 v, int m) {
+    return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
+}
+
+// The rewrite: natural stage -> 4-step runs and permuted B/C.
+__device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid)
+{
+    constexpr int DPB = W8_DPB, NROWF = W8Shape::NROWF, QF = W8Shape::QF, PF = W8Shape::PF;
+    // x, dt, dy: der[a][q][c][k] = arr_a[4q + k][c]
+    for (int e = tid; e < 3 * 2 * DPB; e += W8_THREADS) {
+        const int a = e / (2 * DPB), q = (e / DPB) & 1, cc = e % DPB;
+        const float *src = nat + (4 * q) * NROWF + a * DPB + cc;
+        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) =
+            make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+    }
+    // B, C: der[3QF + a*PF + (i*8 + tau)*16 + 8h + r] = arr_a[i][8h + (r ^ tau)]
+    for (int e = tid; e < 2 * W8_CH * 8 * 4; e += W8_THREADS) {
+        const int q4 = e & 3;                       // float4 within the 16 outputs
+        const int tau = (e >> 2) & 7;
+        const int i = (e >> 5) & 7;
+        const int a = e >> 8;
+        const int h = q4 >> 1, r0 = (q4 & 1) * 4;
+        const float *src = nat + i * NROWF + 3 * DPB + a * 16 + 8 * h;
+        *reinterpret_cast<float4 *>(der + 3 * QF + a * PF + (i * 8 + tau) * 16 + 4 * q4) =
+            make_float4(src[(r0 + 0) ^ tau], src[(r0 + 1) ^ tau], src[(r0 + 2) ^ tau],
+                        src[(r0 + 3) ^ tau]);
+    }
+}
+
+struct W8Lane {
+    int tid, lane, warp, h, c, d0, d, b, tau, kbit;
+    bool dval;
+    float2 an2[4];                 // Aneg * log2(e), lane state order
+    __device__ W8Lane(const float *aneg, int D, int N) {
+        tid = threadIdx.x;
+        lane = tid & 31;
+        warp = tid >> 5;
+        h = tid & 1;
+        c = tid >> 1;
+        d0 = blockIdx.x * W8_DPB;
+        d = d0 + c;
+        b = blockIdx.y;
+        tau = (lane >> 2) & 7;
+        kbit = (lane >> 1) & 1;
+        dval = d < D;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            float v0 = 0.f, v1 = 0.f;
+            const int s0 = 8 * h + ((2 * p) ^ tau), s1 = 8 * h + ((2 * p + 1) ^ tau);
+            if (dval && s0 < N) v0 = __ldg(aneg + (size_t)d * N + s0) * MMS_LOG2E;
+            if (dval && s1 < N) v1 = __ldg(aneg + (size_t)d * N + s1) * MMS_LOG2E;
+            an2[p] = f2(v0, v1);
+        }
+    }
+    // the lane's 8 states (lane order) from a row of n floats (states >= n read as 0)
+    __device__ void load8(float2 (&v)[4], const float *row, int n) const {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int s0 = 8 * h + ((2 * p) ^ tau), s1 = 8 * h + ((2 * p + 1) ^ tau);
+            v[p] = f2(s0 < n ? row[s0] : 0.f, s1 < n ? row[s1] : 0.f);
+        }
+    }
+};
+
+struct W8View {
+    const float *qx, *qdt, *qdy, *pB, *pC;
+    __device__ W8View(const float *der, const W8Lane &L) {
+        qx = der + L.c * 4;
+        qdt = der + W8Shape::QF + L.c * 4;
+        qdy = der + 2 * W8Shape::QF + L.c * 4;
+        pB = der + 3 * W8Shape::QF + L.tau * 16 + 8 * L.h;
+        pC = pB + W8Shape::PF;
+    }
+    __device__ float4 x4(int q) const { return *reinterpret_cast<const float4 *>(qx + q * W8_DPB * 4); }
+    __device__ float4 dt4(int q) const { return *reinterpret_cast<const float4 *>(qdt + q * W8_DPB * 4); }
+    __device__ float4 dy4(int q) const { return *reinterpret_cast<const float4 *>(qdy + q * W8_DPB * 4); }
+    __device__ float4 B(int i, int half) const {
+        return *reinterpret_cast<const float4 *>(pB + i * 8 * 16 + 4 * half);
+    }
+    __device__ float4 C(int i, int half) const {
+        return *reinterpret_cast<const float4 *>(pC + i * 8 * 16 + 4 * half);
+    }
+};
+
+__device__ __forceinline__ float2 pick(const float4 &a, const float4 &b, int p) {
+    return p == 0 ? lo(a) : p == 1 ? hi(a) : p == 2 ? lo(b) : hi(b);
+}
+
+// h <- 4 steps (quad q of the chunk) from h, states not kept.
+__device__ __forceinline__ void w8_advance(float2 (&h)[4], const W8Lane &L, const W8View &v, int q)
+{
+    const float4 x4 = v.x4(q), d4 = v.dt4(q);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int i = 4 * q + k;
+        const float dtv = comp(d4, k), bx = dtv * comp(x4, k);
+        const float4 B0 = v.B(i, 0), B1 = v.B(i, 1);
+        const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+            h[p] = fma2(ex2x2(mul2(md, L.an2[p])), h[p], mul2(bx2, pick(B0, B1, p)));
+    }
+}
+
+struct W8Adj {
+    float2 gad[4], anx[4], dac[4];
+};
+
+// Rebuild quad q from hb, then walk it backwards.
+template <bool FULL>
+__device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], const W8Lane &L,
+                                        W8Adj &A, int q, int nv, float *outq, int D, float *sd)
+{
+    float2 hv[4][4];
+    {
+        const float4 x4 = v.x4(q), d4 = v.dt4(q);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = 4 * q + k;
+            const float dtv = comp(d4, k), bx = dtv * comp(x4, k);
+            const float4 B0 = v.B(i, 0), B1 = v.B(i, 1);
+            const float2 md = f2(-dtv, -dtv), bx2 = f2(bx, bx);
+#pragma unroll
+            for (int p = 0; p < 4; ++p)
+                hv[k][p] = fma2(ex2x2(mul2(md, L.an2[p])), k ? hv[k > 0 ? k - 1 : 0][p] : hb[p],
+                                mul2(bx2, pick(B0, B1, p)));
+        }
+    }
+    const float4 x4 = v.x4(q), d4 = v.dt4(q), y4 = v.dy4(q);
+#pragma unroll
+    for (int k = 3; k >= 0; --k) {
+        const int i = 4 * q + k;
+        if (!FULL && i >= nv) continue;                       // uniform
+        const float dtv = comp(d4, k), xv = comp(x4, k), dyv = comp(y4, k);
+        const float4 B0 = v.B(i, 0), B1 = v.B(i, 1), C0 = v.C(i, 0), C1 = v.C(i, 1);
+        const float2 dy2 = f2(dyv, dyv), dt2 = f2(dtv, dtv), md = f2(-dtv, -dtv);
+        const float dxv = dtv * xv;
+        const float2 dxv2 = f2(dxv, dxv);
+        float2 p1 = f2(0.f, 0.f), p2 = f2(0.f, 0.f), vb[4], vc[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const float2 am = mul2(md, L.an2[p]);
+            const float2 ai = f2(ex2_fresh(am.x), ex2_fresh(am.y));
+            A.gad[p] = fma2(A.anx[p], A.gad[p], mul2(dy2, pick(C0, C1, p)));
+            A.anx[p] = ai;
+            const float2 hp = k ? hv[k > 0 ? k - 1 : 0][p] : hb[p];
+            const float2 u = mul2(A.gad[p], mul2(ai, hp));
+            p1 = fma2(A.gad[p], pick(B0, B1, p), p1);
+            p2 = fma2(L.an2[p], u, p2);
+            A.dac[p] = fma2(dt2, u, A.dac[p]);
+            vb[p] = mul2(A.gad[p], dxv2);
+            vc[p] = mul2(dy2, hv[k][p]);
+        }
+        {   // dx = dt*sum_n g*B, ddt = x*sum_n g*B - sum_n Aneg*u over both lanes of the channel
+            const float s1 = p1.x + p1.y, s2 = p2.x + p2.y;
+            const float v0 = dtv * s1, v1 = fmaf(xv, s1, -W8_LN2 * s2);
+            float keep = L.h ? v1 : v0;
+            keep += __shfl_xor_sync(0xffffffffu, L.h ? v0 : v1, 1);
+            if (L.dval) outq[(size_t)k * D] = keep;
+        }
+        // dB|dC over the warp's 16 channels
+        vb[0] = add2(vb[0], shfl2x(vb[2], 16));
+        vb[1] = add2(vb[1], shfl2x(vb[3], 16));
+        vc[0] = add2(vc[0], shfl2x(vc[2], 16));
+        vc[1] = add2(vc[1], shfl2x(vc[3], 16));
+        vb[0] = add2(vb[0], shfl2x(vb[1], 8));
+        vc[0] = add2(vc[0], shfl2x(vc[1], 8));
+        const float2 bc = add2(f2(vb[0].x, vc[0].x),
+                               f2(__shfl_xor_sync(0xffffffffu, vb[0].y, 4),
+                                  __shfl_xor_sync(0xffffffffu, vc[0].y, 4)));
+        float keep = L.kbit ? bc.y : bc.x;
+        keep += __shfl_xor_sync(0xffffffffu, L.kbit ? bc.x : bc.y, 2);
+        sd[(i * W8_WARPS + L.warp) * 32 + L.kbit * 16 + 8 * L.h + L.tau] = keep;
+    }
+}
+
+#ifndef MMS_BWD_W8_MINB
+#define MMS_BWD_W8_MINB 4
+#endif
+
+template <bool VEC>
+__global__ void __launch_bounds__(W8_THREADS, MMS_BWD_W8_MINB)
+bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
+              const float *__restrict__ aneg, const float *__restrict__ Bm,
+              const float *__restrict__ Cm, const float *__restrict__ dy,
+              const float *__restrict__ ckpt, float *__restrict__ dx,
+              float *__restrict__ ddt, float *__restrict__ part_bc,
+              float *__restrict__ part_a, const float *__restrict__ seg_e,
+              int T, int D, int N, int nblk, int cps)
+{
+    constexpr int DPB = W8_DPB;
+    extern __shared__ __align__(16) float smem[];
+    float *nat = smem;                                     // [W8_NAT][STAGEF]
+    float *der = nat + W8_NAT * W8Shape::STAGEF;           // [DERF]
+    float *sd = der + W8Shape::DERF;                       // [CH][WARPS][32]
+
+    const W8Lane L(aneg, D, N);
+    const int tid = L.tid;
+    const int nchunk = (T + W8_CH - 1) / W8_CH;
+    const size_t plane = (size_t)D * N;
+    const size_t rowD = (size_t)L.b * T * D;
+    const float *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
+    const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
+    const float *ckb = ckpt + (size_t)L.b * nchunk * plane;
+    float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
+
+    // inputs of chunk c and the checkpoint it starts from (zeros for c == 0)
+    auto stage = [&](int buf, int c) {
+        float *st = nat + buf * W8Shape::STAGEF;
+        stage_tile<3, 2, DPB, 16, W8_CH, W8_THREADS, VEC>(st, xb, dtb, dyb, Bb, Cb, c * W8_CH,
+                                                          min(W8_CH, T - c * W8_CH), L.d0, D, N, tid);
+        float *cks = st + W8Shape::NATF;
+        for (int k = tid; k < DPB * 4; k += W8_THREADS) {
+            const int cc = k >> 2, q = k & 3;
+            const bool ok = c >= 1 && L.d0 + cc < D && 4 * q < N;
+            const float *src = ok ? ckb + (size_t)(c - 1) * plane + (size_t)(L.d0 + cc) * N + 4 * q : ckb;
+            cp16(cks + cc * 16 + 4 * q, src, ok);
+        }
+    };
+
+    const int sg = blockIdx.z, nsg = gridDim.z;
+    const int clo = sg * cps, chi = min((sg + 1) * cps, nchunk) - 1;
+    const int nch = chi - clo + 1;
+
+    W8Adj A;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
+    if (sg + 1 < nsg) {                                    // carry from the later segments
+        if (L.dval) L.load8(A.gad, seg_e + ((size_t)L.b * nsg + sg) * plane + (size_t)L.d * N, N);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) A.anx[p] = f2(1.f, 1.f);
+    }
+
+    stage(0, chi);
+    cp_commit();
+    if (nch > 1) stage(1, chi - 1);
+    cp_commit();
+
+    for (int it = 0; it < nch; ++it) {
+        const int c = chi - it;
+        cp_wait<1>();
+        __syncthreads();                                   // chunk c staged; chunk c+1 walked
+        if (it > 0) {                                      // dB|dC partial of chunk c+1
+            const int t0p = (c + 1) * W8_CH, nvp = min(W8_CH, T - t0p);
+            for (int p = tid; p < W8_CH * 32; p += W8_THREADS) {
+                const int i = p >> 5, j = p & 31;
+                const int kind = j >> 4, n = j & 15;
+                if (i < nvp && n < N) {
+                    const float *r = sd + i * W8_WARPS * 32 + j;
+                    pbc[(size_t)(t0p + i) * 2 * N + kind * N + n] = (r[0] + r[32]) + (r[64] + r[96]);
+                }
+            }
+        }
+        const float *st = nat + (it % W8_NAT) * W8Shape::STAGEF;
+        w8_rewrite(st, der, tid);
+        float2 hA[4];
+        L.load8(hA, st + W8Shape::NATF + L.c * 16, 16);
+        if (c - 2 >= clo) stage((it + 2) % W8_NAT, c - 2);
+        cp_commit();
+        __syncthreads();                                   // der ready, sd free
+
+        const W8View v(der, L);
+        const int t0 = c * W8_CH;
+        const int nv = min(W8_CH, T - t0);
+        float *outb = (L.h ? ddt : dx) + rowD + (size_t)t0 * D + L.d;
+        // later group (steps 4..7) from the state after step 3, then the first group
+        if (nv > 4) {
+            float2 h4[4] = {hA[0], hA[1], hA[2], hA[3]};
+            w8_advance(h4, L, v, 0);
+            if (nv == W8_CH) w8_walk<true>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd);
+            else w8_walk<false>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd);
+            w8_walk<true>(v, hA, L, A, 0, nv, outb, D, sd);
+        } else {
+            w8_walk<false>(v, hA, L, A, 0, nv, outb, D, sd);
+        }
+    }
+    cp_wait<0>();
+    __syncthreads();
+    {
+        const int t0p = clo * W8_CH, nvp = min(W8_CH, T - t0p);
+        for (int p = tid; p < W8_CH * 32; p += W8_THREADS) {
+            const int i = p >> 5, j = p & 31;
+            const int kind = j >> 4, n = j & 15;
+            if (i < nvp && n < N) {
+                const float *r = sd + i * W8_WARPS * 32 + j;
+                pbc[(size_t)(t0p + i) * 2 * N + kind * N + n] = (r[0] + r[32]) + (r[64] + r[96]);
+            }
+        }
+    }
+    if (L.dval) {
+        float *pa = part_a + (((size_t)L.b * nsg + sg) * D + L.d) * N;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            const int s0 = 8 * L.h + ((2 * p) ^ L.tau), s1 = 8 * L.h + ((2 * p + 1) ^ L.tau);
+            if (s0 < N) pa[s0] = -A.dac[p].x;
+            if (s1 < N) pa[s1] = -A.dac[p].y;
+        }
+    }
+}
+
+}  // namespace
+
+bool bwd_w8_applies(int N, int K) { return groups_for(N) == 4 && N > 8 && K == W8_CH; }
+
+cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                          int nblk, SegPlan sp, cudaStream_t stream)
+{
+    const bool vec = vec_ok(a.D, a.x, a.dt, a.dy);
+    auto kern = vec ? bwd_kernel_w8<true> : bwd_kernel_w8<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)W8Shape::SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
+    kern<<<grid, W8_THREADS, W8Shape::SMEM, stream>>>(a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt,
+                                                      a.dx, a.ddt, part_bc, part_a, seg_e, a.T,
+                                                      a.D, a.N, nblk, sp.cps);
+    return cudaGetLastError();
+}
+
+}  // namespace mms

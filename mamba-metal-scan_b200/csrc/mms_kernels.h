@@ -105,6 +105,12 @@ struct SegLocalArgs {
     int Bt, T, D, N, L, s_first, nseg, bplanes, splanes, voff, poff;
 };
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream);
+
+// Backward with 8 states per lane (mms_bwd_w8.cu) for 8 < N <= 16 and K == 8;
+// same workspace regions as the general backward.
+bool bwd_w8_applies(int N, int K);
+cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                          int nblk, SegPlan sp, cudaStream_t stream);
 // forward: chain the segment end states through the checkpoint slots
 cudaError_t launch_seg_combine_fwd(float *ckpt, int Bt, int nchunk, int S, int cps, size_t DN,
                                    cudaStream_t stream);
