@@ -60,7 +60,8 @@ inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
     // Splitting costs a local pass over S-1 segments (about 40 % more work for
     // a fwd+bwd step), which pays only below one CTA per SM.
     if (base >= N_SM) return p;
-    const long long want = (4LL * N_SM + base - 1) / base;
+    // segments for whole waves of the backward (4 CTAs of 64 channels per SM)
+    const long long want = (4LL * N_SM) / base;
     long long cps = (nchunk + want - 1) / want;
     if (cps < 2) cps = 2;                           // the forward keeps P_s in chunk cps-2
     if (cps * K < 64) cps = (64 + K - 1) / K;       // at least 64 steps per segment
