@@ -49,9 +49,11 @@ extern "C" {
 #define MMS_ERR_CUDA 5             /* a kernel launch failed (see cudaGetLastError)      */
 #define MMS_ERR_TOO_LARGE 6        /* mms_bwd_noalloc: the shape needs more scratch than
                                       MMS_NOALLOC_SCRATCH_BYTES                          */
+#define MMS_ERR_TIMEOUT 7          /* a kernel gave up waiting for its own staged copies
+                                      (reported by mms_device_status)                    */
 
 /* Version of the ABI in this header (major * 100 + minor). */
-#define MMS_ABI_VERSION 100
+#define MMS_ABI_VERSION 101
 int mms_abi_version(void);
 
 /* Human-readable text for an MMS_* status. Never NULL. */
@@ -126,6 +128,17 @@ int mms_bwd_noalloc(const float *x, const float *dt, const float *aneg,
 int mms_step(const float *x, const float *dt, const float *aneg,
              const float *B, const float *C, float *h, float *y,
              int Bt, int D, int N, void *stream);
+
+/*
+ * Device-side status of the kernels launched so far, for failure detection.
+ * The backward's TMA staging waits on completion barriers with a bounded
+ * poll; a wait that runs out records a flag instead of hanging the GPU (the
+ * results of that call are then wrong). Returns MMS_ERR_TIMEOUT if the flag
+ * was set since the previous call (and clears it), MMS_ERR_CUDA if it cannot
+ * be read, else MMS_OK. Synchronises the device.
+ * No counterpart in the reference (its Metal launches cannot time out).
+ */
+int mms_device_status(void);
 
 #ifdef __cplusplus
 }

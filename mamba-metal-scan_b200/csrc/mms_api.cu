@@ -37,6 +37,7 @@ const char *mms_status_string(int status)
     case MMS_ERR_WORKSPACE: return "workspace missing or smaller than mms_bwd_workspace_size()";
     case MMS_ERR_MISALIGNED: return "misaligned pointer (B, C, Aneg, ckpt, dB, dC, dAneg need 16 bytes)";
     case MMS_ERR_CUDA: return "CUDA launch failed";
+    case MMS_ERR_TIMEOUT: return "a kernel timed out waiting for its staged copies (results invalid)";
     case MMS_ERR_TOO_LARGE:
         return "shape needs more workspace than mms_bwd_noalloc's static scratch "
                "(MMS_NOALLOC_SCRATCH_BYTES = 16 MiB); use mms_bwd with a caller workspace";
@@ -98,6 +99,13 @@ int mms_step(const float *x, const float *dt, const float *aneg, const float *B,
     mms::StepArgs a{x, dt, aneg, B, C, h, y, Bt, D, N};
     return mms::launch_step(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
                                                                                   : MMS_ERR_CUDA;
+}
+
+int mms_device_status(void)
+{
+    if (cudaDeviceSynchronize() != cudaSuccess) return MMS_ERR_CUDA;
+    const int t = mms::w8_take_timeout();
+    return t < 0 ? MMS_ERR_CUDA : t ? MMS_ERR_TIMEOUT : MMS_OK;
 }
 
 }  // extern "C"

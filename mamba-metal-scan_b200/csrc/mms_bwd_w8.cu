@@ -30,6 +30,13 @@
 //     adds the CTAs);
 //   * dAneg: register sums over the walk, one partial per (batch row, time
 //     segment).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <string.h>
+
+#include <mutex>
+
 #include "mms_common.cuh"
 #include "mms_kernels.h"
 #include "mms_stage.cuh"
@@ -45,6 +52,54 @@ constexpr int W8_CH = 8;                        // steps per chunk (the checkpoi
 constexpr int W8_NAT = 3;                       // natural-layout stages
 constexpr float W8_LN2 = 0.6931471805599453f;
 
+// Set when a wait on a TMA completion barrier gave up (see w8_wait);
+// read and cleared by mms_device_status().
+__device__ unsigned int g_w8_timeout;
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+                 " selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait for a stage's copies: after 2^22 polls (each may suspend
+// briefly in hardware) the thread records a timeout and goes on, so a lost
+// copy turns into an error status instead of a hung GPU.
+__device__ __forceinline__ void w8_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try(bar, parity)) return;
+    atomicOr(&g_w8_timeout, 1u);
+}
+// TMA tile loads (no multicast) that complete on an mbarrier.
+__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap *m, int c0, int c1, int c2,
+                                     uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4}], [%5];\n"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap *m, int c0, int c1, int c2,
+                                     int c3, uint32_t bar) {
+    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+                 " [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+                   "r"(bar)
+                 : "memory");
+}
+
+// The six tensor maps of the TMA staging path.
+struct W8Maps {
+    CUtensorMap x, dt, dy, B, C, ck;
+};
+
 struct W8Shape {
     static constexpr int NROWF = 3 * W8_DPB + 2 * 16;          // x, dt, dy, B, C per step
     static constexpr int NATF = W8_CH * NROWF;
@@ -55,22 +110,37 @@ struct W8Shape {
     static constexpr int DERF = 3 * QF + 2 * PF;
     static constexpr int SDF = W8_CH * W8_WARPS * 32;          // per-warp dB|dC sums
     static constexpr size_t SMEM = sizeof(float) * ((size_t)W8_NAT * STAGEF + DERF + SDF);
+    // TMA layout of a stage (array-major, every region 128-byte aligned):
+    // x, dt, dy [CH][DPB], B, C [CH][16], entry slab [DPB][16]; same size.
+    static constexpr int T_ARR = W8_CH * W8_DPB;               // floats per channel array
+    static constexpr int T_BC = 3 * T_ARR;
+    static constexpr int T_CK = T_BC + 2 * W8_CH * 16;
+    static constexpr uint32_t T_BYTES = 4u * (T_CK + W8_DPB * 16);
+    static constexpr size_t SMEM_TMA = SMEM + 64;             // + the stage barriers
 };
+static_assert(W8Shape::T_CK + W8_DPB * 16 == W8Shape::STAGEF, "stage layouts differ in size");
 
 __device__ __forceinline__ float2 shfl2x(float2 v, int m) {
     return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-// The rewrite: natural stage -> 4-step runs and permuted B/C.
+// The rewrite: staged tile -> 4-step runs and permuted B/C. TMA selects the
+// stage layout: array-major (TMA) or one interleaved row per step (cp.async).
+template <bool TMA>
 __device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid)
 {
     constexpr int DPB = W8_DPB, NROWF = W8Shape::NROWF, QF = W8Shape::QF, PF = W8Shape::PF;
+    constexpr int AROW = TMA ? DPB : NROWF;                      // step stride, channel arrays
+    constexpr int AOFF = TMA ? W8Shape::T_ARR : DPB;             // array stride
+    constexpr int BROW = TMA ? 16 : NROWF;                       // step stride, B and C
+    constexpr int BOFF = TMA ? W8Shape::T_BC : 3 * DPB;
+    constexpr int BARR = TMA ? W8_CH * 16 : 16;                  // B -> C
     // x, dt, dy: der[a][q][c][k] = arr_a[4q + k][c]
     for (int e = tid; e < 3 * 2 * DPB; e += W8_THREADS) {
         const int a = e / (2 * DPB), q = (e / DPB) & 1, cc = e % DPB;
-        const float *src = nat + (4 * q) * NROWF + a * DPB + cc;
+        const float *src = nat + (4 * q) * AROW + a * AOFF + cc;
         *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) =
-            make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+            make_float4(src[0], src[AROW], src[2 * AROW], src[3 * AROW]);
     }
     // B, C: der[3QF + a*PF + (i*8 + tau)*16 + 8h + r] = arr_a[i][8h + (r ^ tau)]
     for (int e = tid; e < 2 * W8_CH * 8 * 4; e += W8_THREADS) {
@@ -79,7 +149,7 @@ __device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid
         const int i = (e >> 5) & 7;
         const int a = e >> 8;
         const int h = q4 >> 1, r0 = (q4 & 1) * 4;
-        const float *src = nat + i * NROWF + 3 * DPB + a * 16 + 8 * h;
+        const float *src = nat + i * BROW + BOFF + a * BARR + 8 * h;
         *reinterpret_cast<float4 *>(der + 3 * QF + a * PF + (i * 8 + tau) * 16 + 4 * q4) =
             make_float4(src[(r0 + 0) ^ tau], src[(r0 + 1) ^ tau], src[(r0 + 2) ^ tau],
                         src[(r0 + 3) ^ tau]);
@@ -237,7 +307,12 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
 #define MMS_BWD_W8_MINB 4
 #endif
 
-template <bool VEC>
+// VEC: 16-byte cp.async staging (D % 4 == 0, aligned arrays). TMA: the
+// stages are filled by TMA tile loads from the tensor maps in `maps` (one
+// thread issues 6 loads per chunk; out-of-range steps, channels, states and
+// the chunk-0 entry state arrive as zeros) and complete on per-stage
+// mbarriers.
+template <bool VEC, bool TMA>
 __global__ void __launch_bounds__(W8_THREADS, MMS_BWD_W8_MINB)
 bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
@@ -245,13 +320,14 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ ckpt, float *__restrict__ dx,
               float *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
-              int T, int D, int N, int nblk, int cps)
+              int T, int D, int N, int nblk, int cps, const __grid_constant__ W8Maps maps)
 {
     constexpr int DPB = W8_DPB;
-    extern __shared__ __align__(16) float smem[];
+    extern __shared__ __align__(128) float smem[];
     float *nat = smem;                                     // [W8_NAT][STAGEF]
     float *der = nat + W8_NAT * W8Shape::STAGEF;           // [DERF]
     float *sd = der + W8Shape::DERF;                       // [CH][WARPS][32]
+    const uint32_t bars = smem_u32(sd + W8Shape::SDF);     // TMA: W8_NAT stage barriers
 
     const W8Lane L(aneg, D, N);
     const int tid = L.tid;
@@ -266,6 +342,20 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
     // inputs of chunk c and the checkpoint it starts from (zeros for c == 0)
     auto stage = [&](int buf, int c) {
         float *st = nat + buf * W8Shape::STAGEF;
+        if constexpr (TMA) {
+            if (tid == 0) {
+                const uint32_t bar = bars + 8 * buf, dst = smem_u32(st);
+                mbar_expect(bar, W8Shape::T_BYTES);
+                const int t0 = c * W8_CH;
+                tma3(dst, &maps.x, L.d0, t0, L.b, bar);
+                tma3(dst + 4 * W8Shape::T_ARR, &maps.dt, L.d0, t0, L.b, bar);
+                tma3(dst + 8 * W8Shape::T_ARR, &maps.dy, L.d0, t0, L.b, bar);
+                tma3(dst + 4 * W8Shape::T_BC, &maps.B, 0, t0, L.b, bar);
+                tma3(dst + 4 * (W8Shape::T_BC + W8_CH * 16), &maps.C, 0, t0, L.b, bar);
+                tma4(dst + 4 * W8Shape::T_CK, &maps.ck, 0, L.d0, c - 1, L.b, bar);
+            }
+            return;
+        }
         stage_tile<3, 2, DPB, 16, W8_CH, W8_THREADS, VEC>(st, xb, dtb, dyb, Bb, Cb, c * W8_CH,
                                                           min(W8_CH, T - c * W8_CH), L.d0, D, N, tid);
         float *cks = st + W8Shape::NATF;
@@ -290,6 +380,13 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
         for (int p = 0; p < 4; ++p) A.anx[p] = f2(1.f, 1.f);
     }
 
+    if constexpr (TMA) {
+        if (tid == 0) {
+            for (int s2 = 0; s2 < W8_NAT; ++s2) mbar_init(bars + 8 * s2, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        }
+        __syncthreads();
+    }
     stage(0, chi);
     cp_commit();
     if (nch > 1) stage(1, chi - 1);
@@ -297,7 +394,8 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
 
     for (int it = 0; it < nch; ++it) {
         const int c = chi - it;
-        cp_wait<1>();
+        if constexpr (TMA) w8_wait(bars + 8 * (it % W8_NAT), (it / W8_NAT) & 1);
+        else cp_wait<1>();
         __syncthreads();                                   // chunk c staged; chunk c+1 walked
         if (it > 0) {                                      // dB|dC partial of chunk c+1
             const int t0p = (c + 1) * W8_CH, nvp = min(W8_CH, T - t0p);
@@ -311,10 +409,14 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
             }
         }
         const float *st = nat + (it % W8_NAT) * W8Shape::STAGEF;
-        w8_rewrite(st, der, tid);
+        w8_rewrite<TMA>(st, der, tid);
         float2 hA[4];
-        L.load8(hA, st + W8Shape::NATF + L.c * 16, 16);
-        if (c - 2 >= clo) stage((it + 2) % W8_NAT, c - 2);
+        L.load8(hA, st + (TMA ? W8Shape::T_CK : W8Shape::NATF) + L.c * 16, 16);
+        if (c - 2 >= clo) {
+            // the stage's previous chunk was read before the barrier above
+            if (TMA && tid == 0) fence_async_smem();
+            stage((it + 2) % W8_NAT, c - 2);
+        }
         cp_commit();
         __syncthreads();                                   // der ready, sd free
 
@@ -361,19 +463,98 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
 
 bool bwd_w8_applies(int N, int K) { return groups_for(N) == 4 && N > 8 && K == W8_CH; }
 
+#ifndef MMS_BWD_TMA
+#define MMS_BWD_TMA 1
+#endif
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// fp32 tile map over a row-major array whose innermost `rank` dims are `dim`
+// (dim[0] contiguous), box `box`; out-of-range elements load as zeros.
+bool encode(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap *m, const void *base, int rank,
+            const cuuint64_t *dim, const cuuint32_t *box)
+{
+    cuuint64_t stride[4];
+    cuuint64_t s = 4;
+    for (int i = 0; i + 1 < rank; ++i) {
+        s *= dim[i];
+        stride[i] = s;
+    }
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void *>(base), dim, stride, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool build_maps(const BwdArgs &a, W8Maps *m)
+{
+    const auto fn = tensor_map_encoder();
+    if (!fn) return false;
+    const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
+    const cuuint32_t bX[3] = {W8_DPB, W8_CH, 1};
+    const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
+    const cuuint32_t bB[3] = {16, W8_CH, 1};
+    const int nchunk = (a.T + W8_CH - 1) / W8_CH;
+    const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
+    const cuuint32_t bK[4] = {16, W8_DPB, 1, 1};
+    return encode(fn, &m->x, a.x, 3, dX, bX) && encode(fn, &m->dt, a.dt, 3, dX, bX) &&
+           encode(fn, &m->dy, a.dy, 3, dX, bX) && encode(fn, &m->B, a.B, 3, dB, bB) &&
+           encode(fn, &m->C, a.C, 3, dB, bB) && encode(fn, &m->ck, a.ckpt, 4, dK, bK);
+}
+
+template <bool VEC, bool TMA>
+cudaError_t launch_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                      int nblk, SegPlan sp, const W8Maps &maps, cudaStream_t stream)
+{
+    const size_t smem = TMA ? W8Shape::SMEM_TMA : W8Shape::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(bwd_kernel_w8<VEC, TMA>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
+    bwd_kernel_w8<VEC, TMA><<<grid, W8_THREADS, smem, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e, a.T, a.D,
+        a.N, nblk, sp.cps, maps);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                           int nblk, SegPlan sp, cudaStream_t stream)
 {
-    const bool vec = vec_ok(a.D, a.x, a.dt, a.dy);
-    auto kern = vec ? bwd_kernel_w8<true> : bwd_kernel_w8<false>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)W8Shape::SMEM);
-    if (e != cudaSuccess) return e;
-    dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
-    kern<<<grid, W8_THREADS, W8Shape::SMEM, stream>>>(a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt,
-                                                      a.dx, a.ddt, part_bc, part_a, seg_e, a.T,
-                                                      a.D, a.N, nblk, sp.cps);
-    return cudaGetLastError();
+    W8Maps maps;
+    memset(&maps, 0, sizeof(maps));
+    if (!vec_ok(a.D, a.x, a.dt, a.dy))
+        return launch_w8<false, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
+    if (MMS_BWD_TMA && build_maps(a, &maps))
+        return launch_w8<true, true>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
+    return launch_w8<true, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
+}
+
+int w8_take_timeout()
+{
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_w8_timeout, sizeof(v)) != cudaSuccess) return -1;
+    if (v) {
+        const unsigned int z = 0;
+        cudaMemcpyToSymbol(g_w8_timeout, &z, sizeof(z));
+    }
+    return v ? 1 : 0;
 }
 
 }  // namespace mms

@@ -22,6 +22,7 @@ MMS_ERR_WORKSPACE = 3
 MMS_ERR_MISALIGNED = 4
 MMS_ERR_CUDA = 5
 MMS_ERR_TOO_LARGE = 6
+MMS_ERR_TIMEOUT = 7
 
 # Every symbol include/mms_scan.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -34,6 +35,7 @@ SIGNATURES = {
     "mms_bwd": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
     "mms_bwd_noalloc": ([_P] * 12 + [_I] * 5 + [_P], _I),
     "mms_step": ([_P] * 7 + [_I] * 3 + [_P], _I),
+    "mms_device_status": ([], _I),
 }
 
 _lib = None
@@ -129,3 +131,8 @@ def step(x, dt, aneg, b_in, c_in, h):
                       bt, d, n, _stream(x.device))
     _check(rc, "mms_step")
     return y
+
+
+def device_status() -> int:
+    """MMS_OK, or MMS_ERR_TIMEOUT if a kernel's bounded wait ran out since the last call."""
+    return int(load().mms_device_status())

@@ -37,9 +37,9 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _native.load()
-    assert lib.mms_abi_version() == 100
-    for rc in range(6):
-        assert _native.status_string(rc)
+    assert lib.mms_abi_version() == 101
+    for rc in range(8):
+        assert _native.status_string(rc) != "unknown status"
     assert _native.status_string(99) == "unknown status"
 
 

@@ -345,3 +345,11 @@ def test_recurrent_cache_matches_full_recomputation_on_cuda():
                  for t in range(step.shape[1])]
     for a, b in zip(cached, naive):
         assert torch.allclose(a, b, atol=1e-5)
+
+
+def test_no_kernel_reported_a_timeout():
+    """The backward's TMA stages wait on barriers with a bounded poll; none ran out."""
+    from mamba_metal import _native
+    x, dt, aneg, b_in, c_in, dy = inputs(16, 512, 2304, 16, "c0", seed=9, device=DEV)
+    cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=8)
+    assert _native.device_status() == _native.MMS_OK
