@@ -104,8 +104,9 @@ int mms_step(const float *x, const float *dt, const float *aneg, const float *B,
 int mms_device_status(void)
 {
     if (cudaDeviceSynchronize() != cudaSuccess) return MMS_ERR_CUDA;
-    const int t = mms::w8_take_timeout();
-    return t < 0 ? MMS_ERR_CUDA : t ? MMS_ERR_TIMEOUT : MMS_OK;
+    const int t = mms::w8_take_timeout(), f = mms::fwd_take_timeout();
+    if (t < 0 || f < 0) return MMS_ERR_CUDA;
+    return t || f ? MMS_ERR_TIMEOUT : MMS_OK;
 }
 
 }  // extern "C"

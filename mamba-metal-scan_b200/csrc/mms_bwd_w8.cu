@@ -30,16 +30,12 @@
 //     adds the CTAs);
 //   * dAneg: register sums over the walk, one partial per (batch row, time
 //     segment).
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <string.h>
-
-#include <mutex>
 
 #include "mms_common.cuh"
 #include "mms_kernels.h"
 #include "mms_stage.cuh"
+#include "mms_tma.cuh"
 
 namespace mms {
 
@@ -56,20 +52,6 @@ constexpr float W8_LN2 = 0.6931471805599453f;
 // read and cleared by mms_device_status().
 __device__ unsigned int g_w8_timeout;
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-                 " selp.u32 %0, 1, 0, p;\n}\n"
-                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
 // Bounded wait for a stage's copies: after 2^22 polls (each may suspend
 // briefly in hardware) the thread records a timeout and goes on, so a lost
 // copy turns into an error status instead of a hung GPU.
@@ -78,23 +60,6 @@ __device__ __forceinline__ void w8_wait(uint32_t bar, uint32_t parity) {
         if (mbar_try(bar, parity)) return;
     atomicOr(&g_w8_timeout, 1u);
 }
-// TMA tile loads (no multicast) that complete on an mbarrier.
-__device__ __forceinline__ void tma3(uint32_t dst, const CUtensorMap *m, int c0, int c1, int c2,
-                                     uint32_t bar) {
-    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3, %4}], [%5];\n"
-                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap *m, int c0, int c1, int c2,
-                                     int c3, uint32_t bar) {
-    asm volatile("cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-                 " [%0], [%1, {%2, %3, %4, %5}], [%6];\n"
-                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
-                   "r"(bar)
-                 : "memory");
-}
-
 // The six tensor maps of the TMA staging path.
 struct W8Maps {
     CUtensorMap x, dt, dy, B, C, ck;
@@ -469,41 +434,9 @@ bool bwd_w8_applies(int N, int K) { return groups_for(N) == 4 && N > 8 && K == W
 
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
-{
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-                cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// fp32 tile map over a row-major array whose innermost `rank` dims are `dim`
-// (dim[0] contiguous), box `box`; out-of-range elements load as zeros.
-bool encode(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap *m, const void *base, int rank,
-            const cuuint64_t *dim, const cuuint32_t *box)
-{
-    cuuint64_t stride[4];
-    cuuint64_t s = 4;
-    for (int i = 0; i + 1 < rank; ++i) {
-        s *= dim[i];
-        stride[i] = s;
-    }
-    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void *>(base), dim, stride, box,
-              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 bool build_maps(const BwdArgs &a, W8Maps *m)
 {
-    const auto fn = tensor_map_encoder();
+    const auto fn = tma_encoder();
     if (!fn) return false;
     const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
     const cuuint32_t bX[3] = {W8_DPB, W8_CH, 1};
@@ -512,9 +445,9 @@ bool build_maps(const BwdArgs &a, W8Maps *m)
     const int nchunk = (a.T + W8_CH - 1) / W8_CH;
     const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
     const cuuint32_t bK[4] = {16, W8_DPB, 1, 1};
-    return encode(fn, &m->x, a.x, 3, dX, bX) && encode(fn, &m->dt, a.dt, 3, dX, bX) &&
-           encode(fn, &m->dy, a.dy, 3, dX, bX) && encode(fn, &m->B, a.B, 3, dB, bB) &&
-           encode(fn, &m->C, a.C, 3, dB, bB) && encode(fn, &m->ck, a.ckpt, 4, dK, bK);
+    return tma_encode(fn, &m->x, a.x, 3, dX, bX) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX) &&
+           tma_encode(fn, &m->dy, a.dy, 3, dX, bX) && tma_encode(fn, &m->B, a.B, 3, dB, bB) &&
+           tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
 template <bool VEC, bool TMA>

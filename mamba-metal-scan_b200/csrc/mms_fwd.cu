@@ -16,9 +16,12 @@
 // recurrence never waits on DRAM. y_t needs the sum over the channel's G
 // lanes: each lane stores its partial in shared memory and, once per tile,
 // every thread finishes some (t, d) sums and writes y with coalesced stores.
+#include <string.h>
+
 #include "mms_common.cuh"
 #include "mms_kernels.h"
 #include "mms_stage.cuh"
+#include "mms_tma.cuh"
 
 namespace mms {
 
@@ -44,7 +47,7 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 {
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
-    extern __shared__ __align__(16) float smem[];
+    extern __shared__ __align__(128) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
     float *ys = smem + FWD_STAGES * TT * ROWF;             // [TT][DPB][G] partial y
 
@@ -178,20 +181,48 @@ struct S16Shape {
     static constexpr size_t CKF = (size_t)2 * 2 * DPB * 16;  // [2][2][DPB*N]
     static constexpr size_t SMEM = sizeof(float) * TILEF;
     static constexpr size_t SMEM_BULK = sizeof(float) * (TILEF + YF + CKF);
+    static constexpr size_t SMEM_TMA = SMEM_BULK + 64;       // + the stage barriers
+    static constexpr uint32_t TILE_BYTES = sizeof(float) * S16_TT * ROWF;
 };
 
-template <bool VEC, bool BULK>
+// Tensor maps of the TMA staging path: x, dt (D, T, Bt) with 128 x 16 boxes,
+// B, C (N, T, Bt) with 16 x 16 boxes.
+struct FwdMaps {
+    CUtensorMap x, dt, B, C;
+};
+
+// Set when a wait on a forward TMA stage gave up; read by mms_device_status().
+__device__ unsigned int g_fwd_timeout;
+
+__device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); ++i)
+        if (mbar_try(bar, parity)) return;
+    atomicOr(&g_fwd_timeout, 1u);
+}
+
+// TMA: tiles arrive by TMA tile loads (one thread, 4 per tile) that complete
+// on per-stage mbarriers, in an array-major layout [x TTxDPB][dt TTxDPB]
+// [B TTx16][C TTx16]; out-of-range steps, channels and states load as zeros,
+// like the cp.async path's zero fill.
+template <bool VEC, bool BULK, bool TMA>
 __global__ void __launch_bounds__(S16_DPB, 2)
 fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, float *__restrict__ y,
-               float *__restrict__ ckpt, int T, int D, int N, int K)
+               float *__restrict__ ckpt, int T, int D, int N, int K,
+               const __grid_constant__ FwdMaps maps)
 {
     constexpr int DPB = S16Shape::DPB, ROWF = S16Shape::ROWF, TT = S16_TT;
-    extern __shared__ __align__(16) float smem[];
+    // where step j of a tile keeps x, dt, B, C (floats from the tile start)
+    constexpr int XROW = TMA ? DPB : ROWF, XOFF = 0;
+    constexpr int DOFF = TMA ? TT * DPB : DPB;
+    constexpr int BROW = TMA ? 16 : ROWF, BOFF = TMA ? 2 * TT * DPB : 2 * DPB;
+    constexpr int COFF = TMA ? 2 * TT * DPB + TT * 16 : 2 * DPB + 16;
+    extern __shared__ __align__(128) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
     float *ys = smem + S16Shape::TILEF;                    // BULK: [2][TT][DPB]
     float *cks = ys + S16Shape::YF;                        // BULK: [2][2][DPB*N]
+    const uint32_t bars = smem_u32(cks + S16Shape::CKF);   // TMA: FWD_STAGES barriers
 
     const int tid = threadIdx.x;
     const int d0 = blockIdx.x * DPB;
@@ -232,12 +263,35 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         bulk_commit();
     };
 
+    // stage tile kt into buffer buf
+    auto stage = [&](int buf, int kt) {
+        float *tile = tiles + buf * TT * ROWF;
+        if constexpr (TMA) {
+            if (tid == 0) {
+                const uint32_t bar = bars + 8 * buf, dst = smem_u32(tile);
+                mbar_expect(bar, S16Shape::TILE_BYTES);
+                tma3(dst, &maps.x, d0, kt * TT, b, bar);
+                tma3(dst + 4 * DOFF, &maps.dt, d0, kt * TT, b, bar);
+                tma3(dst + 4 * BOFF, &maps.B, 0, kt * TT, b, bar);
+                tma3(dst + 4 * COFF, &maps.C, 0, kt * TT, b, bar);
+            }
+        } else {
+            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tile, xb, dtb, dtb, Bb, Cb, kt * TT,
+                                                    min(TT, T - kt * TT), d0, D, N, tid);
+        }
+    };
+
     const int ntiles = (T + TT - 1) / TT;
+    if constexpr (TMA) {
+        if (tid == 0) {
+            for (int s = 0; s < FWD_STAGES; ++s) mbar_init(bars + 8 * s, 1);
+            asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        }
+        __syncthreads();
+    }
 #pragma unroll
     for (int s = 0; s < FWD_STAGES - 1; ++s) {
-        if (s < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
-                                                    s * TT, min(TT, T - s * TT), d0, D, N, tid);
+        if (s < ntiles) stage(s, s);
         cp_commit();
     }
 
@@ -250,16 +304,18 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
             if (k > 0) fence_async_smem();                 // tile k-1's y / checkpoints
             if (tid == 0) bulk_wait_read<0>();             // tile k-2's copies have left set k&1
         }
-        cp_wait<FWD_STAGES - 2>();
+        if constexpr (TMA) fwd_wait(bars + 8 * (k % FWD_STAGES), (k / FWD_STAGES) & 1);
+        else cp_wait<FWD_STAGES - 2>();
         __syncthreads();
         if constexpr (BULK) {
             if (k > 0 && tid == 0) send(k - 1, pnck, pck0, pck1);
         }
         const int kn = k + FWD_STAGES - 1;
-        if (kn < ntiles)
-            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(
-                tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, kn * TT,
-                min(TT, T - kn * TT), d0, D, N, tid);
+        if (kn < ntiles) {
+            // the buffer's previous tile (k-1) was read before the barrier above
+            if (TMA && tid == 0) fence_async_smem();
+            stage(kn % FWD_STAGES, kn);
+        }
         cp_commit();
 
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
@@ -268,17 +324,17 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         nck = 0;
 #pragma unroll 4
         for (int j = 0; j < TT; ++j) {
-            const float *row = tile + j * ROWF;
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = row[tid];
-            const float dtv = row[DPB + tid];
-            const float4 *bc = reinterpret_cast<const float4 *>(row + 2 * DPB);
+            const float xv = tile[XOFF + j * XROW + tid];
+            const float dtv = tile[DOFF + j * XROW + tid];
+            const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW);
+            const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
             const float bx = dtv * xv;
             const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
             float2 acc = f2(0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const float4 Bv = bc[q], Cv = bc[4 + q];
+                const float4 Bv = bp[q], Cv = cp[q];
                 h[2 * q] = fma2(ex2x2(mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
                 h[2 * q + 1] = fma2(ex2x2(mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1], mul2(bx2, hi(Bv)));
                 acc = fma2(lo(Cv), h[2 * q], acc);
@@ -319,30 +375,63 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     }
 }
 
-template <bool VEC, bool BULK>
-static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, cudaStream_t stream)
+template <bool VEC, bool BULK, bool TMA>
+static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
 {
-    const size_t smem = BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK>,
+    const size_t smem = TMA ? S16Shape::SMEM_TMA : BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt);
-    fwd_kernel_s16<VEC, BULK><<<grid, S16_DPB, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K);
+    fwd_kernel_s16<VEC, BULK, TMA><<<grid, S16_DPB, smem, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, maps);
     return cudaGetLastError();
 }
 
 #ifndef MMS_FWD_BULK
 #define MMS_FWD_BULK 1
 #endif
+#ifndef MMS_FWD_TMA
+#define MMS_FWD_TMA 1
+#endif
+
+static bool fwd_maps(const FwdArgs &a, FwdMaps *m)
+{
+    const auto fn = tma_encoder();
+    if (!fn) return false;
+    const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
+    const cuuint32_t bX[3] = {S16_DPB, S16_TT, 1};
+    const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
+    const cuuint32_t bB[3] = {16, S16_TT, 1};
+    return tma_encode(fn, &m->x, a.x, 3, dX, bX) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX) &&
+           tma_encode(fn, &m->B, a.B, 3, dB, bB) && tma_encode(fn, &m->C, a.C, 3, dB, bB);
+}
 
 static cudaError_t launch_fwd_s16(const FwdArgs &a, cudaStream_t stream)
 {
-    // The bulk path needs 16-byte aligned y rows (D % 4 == 0, aligned y) and
-    // suits strides K >= 8 (at most two checkpoints per 16-step tile).
-    if (!vec_ok(a.D, a.x, a.dt)) return launch_fwd_s16_vb<false, false>(a, stream);
-    if (MMS_FWD_BULK && a.K >= 8 && vec_ok(a.D, a.y, a.y)) return launch_fwd_s16_vb<true, true>(a, stream);
-    return launch_fwd_s16_vb<true, false>(a, stream);
+    // The bulk-store path needs 16-byte aligned y rows (D % 4 == 0, aligned y)
+    // and suits strides K >= 8 (at most two checkpoints per 16-step tile); the
+    // TMA-staged variant of it also needs the tensor maps to encode.
+    FwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    if (!vec_ok(a.D, a.x, a.dt)) return launch_fwd_s16_vb<false, false, false>(a, maps, stream);
+    if (MMS_FWD_BULK && a.K >= 8 && vec_ok(a.D, a.y, a.y)) {
+        if (MMS_FWD_TMA && fwd_maps(a, &maps))
+            return launch_fwd_s16_vb<true, true, true>(a, maps, stream);
+        return launch_fwd_s16_vb<true, true, false>(a, maps, stream);
+    }
+    return launch_fwd_s16_vb<true, false, false>(a, maps, stream);
+}
+
+int fwd_take_timeout()
+{
+    unsigned int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_fwd_timeout, sizeof(v)) != cudaSuccess) return -1;
+    if (v) {
+        const unsigned int z = 0;
+        cudaMemcpyToSymbol(g_fwd_timeout, &z, sizeof(z));
+    }
+    return v ? 1 : 0;
 }
 
 template <int G, bool VEC>

@@ -115,6 +115,7 @@ cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const
 // 1 if a TMA-stage wait timed out since the last call (and clears it), 0 if
 // not, -1 if the flag could not be read.
 int w8_take_timeout();
+int fwd_take_timeout();
 // forward: chain the segment end states through the checkpoint slots
 cudaError_t launch_seg_combine_fwd(float *ckpt, int Bt, int nchunk, int S, int cps, size_t DN,
                                    cudaStream_t stream);
