@@ -37,6 +37,10 @@
 #include "mms_stage.cuh"
 #include "mms_tma.cuh"
 
+#ifndef MMS_W8_TREE
+#define MMS_W8_TREE 1
+#endif
+
 namespace mms {
 
 namespace {
@@ -230,7 +234,8 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
         const float2 dy2 = f2(dyv, dyv), dt2 = f2(dtv, dtv), md = f2(-dtv, -dtv);
         const float dxv = dtv * xv;
         const float2 dxv2 = f2(dxv, dxv);
-        float2 p1 = f2(0.f, 0.f), p2 = f2(0.f, 0.f), vb[4], vc[4];
+        float2 p1[2] = {f2(0.f, 0.f), f2(0.f, 0.f)}, p2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+        float2 vb[4], vc[4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
             const float2 am = mul2(md, L.an2[p]);
@@ -239,14 +244,16 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
             A.anx[p] = ai;
             const float2 hp = k ? hv[k > 0 ? k - 1 : 0][p] : hb[p];
             const float2 u = mul2(A.gad[p], mul2(ai, hp));
-            p1 = fma2(A.gad[p], pick(B0, B1, p), p1);
-            p2 = fma2(L.an2[p], u, p2);
+            // two partial sums each (MMS_W8_TREE) instead of one serial chain
+            p1[MMS_W8_TREE ? p & 1 : 0] = fma2(A.gad[p], pick(B0, B1, p), p1[MMS_W8_TREE ? p & 1 : 0]);
+            p2[MMS_W8_TREE ? p & 1 : 0] = fma2(L.an2[p], u, p2[MMS_W8_TREE ? p & 1 : 0]);
             A.dac[p] = fma2(dt2, u, A.dac[p]);
             vb[p] = mul2(A.gad[p], dxv2);
             vc[p] = mul2(dy2, hv[k][p]);
         }
         {   // dx = dt*sum_n g*B, ddt = x*sum_n g*B - sum_n Aneg*u over both lanes of the channel
-            const float s1 = p1.x + p1.y, s2 = p2.x + p2.y;
+            const float2 q1 = add2(p1[0], p1[1]), q2 = add2(p2[0], p2[1]);
+            const float s1 = q1.x + q1.y, s2 = q2.x + q2.y;
             const float v0 = dtv * s1, v1 = fmaf(xv, s1, -W8_LN2 * s2);
             float keep = L.h ? v1 : v0;
             keep += __shfl_xor_sync(0xffffffffu, L.h ? v0 : v1, 1);

@@ -169,6 +169,9 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 // 128 channels x N (each a contiguous block of ckpt), double buffered; a
 // third checkpoint in one tile (only the t = T-1 one can be) is stored
 // directly.
+#ifndef MMS_FWD_ACC
+#define MMS_FWD_ACC 4
+#endif
 constexpr int S16_DPB = 128;                                 // channels (= threads) per CTA
 constexpr int S16_TT = 16;
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
@@ -331,18 +334,23 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
             const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
             const float bx = dtv * xv;
             const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
-            float2 acc = f2(0.f, 0.f);
+            // y = sum_n C*h over MMS_FWD_ACC independent partial sums (shorter chains)
+            float2 acc[MMS_FWD_ACC];
+#pragma unroll
+            for (int q = 0; q < MMS_FWD_ACC; ++q) acc[q] = f2(0.f, 0.f);
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float4 Bv = bp[q], Cv = cp[q];
                 h[2 * q] = fma2(ex2x2(mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
                 h[2 * q + 1] = fma2(ex2x2(mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1], mul2(bx2, hi(Bv)));
-                acc = fma2(lo(Cv), h[2 * q], acc);
-                acc = fma2(hi(Cv), h[2 * q + 1], acc);
+                acc[(2 * q) % MMS_FWD_ACC] = fma2(lo(Cv), h[2 * q], acc[(2 * q) % MMS_FWD_ACC]);
+                acc[(2 * q + 1) % MMS_FWD_ACC] = fma2(hi(Cv), h[2 * q + 1], acc[(2 * q + 1) % MMS_FWD_ACC]);
             }
+#pragma unroll
+            for (int q = 1; q < MMS_FWD_ACC; ++q) acc[0] = add2(acc[0], acc[q]);
             const int t = t0 + j;
-            if constexpr (BULK) yrow[j * DPB] = acc.x + acc.y;
-            else if (dval && t < T) yb[(size_t)t * D] = acc.x + acc.y;
+            if constexpr (BULK) yrow[j * DPB] = acc[0].x + acc[0].y;
+            else if (dval && t < T) yb[(size_t)t * D] = acc[0].x + acc[0].y;
             if (t == next_ck) {                            // uniform across the CTA
                 float *o = ckb + (size_t)chunk * D * N;
                 if (BULK && nck < 2) {
