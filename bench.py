@@ -20,6 +20,7 @@ Printed (rank 0): one JSON line with the contract keys plus
                 buffers, copies in and all outputs back inside the timed region
   train         TinyMamba config 2 (vocab 32768, d_model 640, 12 layers) tok/s
   decode        the one-token step kernel at the config-4 decode shape
+  proj          the scan with the dt / softplus(A) prologue fused into the kernels
   clocks        nvidia-smi samples taken during the timed region
 `--impl reference` times only the reference CPU path (rank 0) and prints its line.
 """
@@ -391,6 +392,8 @@ def run_native(args, shape):
         line["train"] = run_train(args, device)
     if not args.no_decode and world == 1:
         line["decode"] = run_decode(args, device, hbm_gbs)
+    if not args.no_proj and world == 1:
+        line["proj"] = run_proj(args, shape, device)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(shape, args.cpu_budget)
     if rank == 0:
@@ -603,6 +606,54 @@ def run_decode(args, device, hbm_gbs):
             "gpu_launches": launches}
 
 
+def run_proj(args, shape, device):
+    """Row f2: the scan with the model's dt / softplus(A) prologue fused into the
+    kernels (selective_scan_proj) against the same prologue as PyTorch ops
+    before selective_scan, both fwd + autograd bwd through the public API at
+    the bench shape, inputs resident."""
+    from mamba_metal import selective_scan, selective_scan_proj
+    from mamba_metal.scan import proj_ref
+    bt, t_len, d, n, kk = shape
+    g = torch.Generator(device="cpu").manual_seed(3)
+    x = torch.randn(bt, t_len, d, generator=g).to(device)
+    logit = torch.randn(bt, t_len, d, generator=g).to(device)
+    a = (torch.arange(1, n + 1).float().repeat(d, 1) - 2.0).to(device)
+    b_in = torch.randn(bt, t_len, n, generator=g).to(device)
+    c_in = torch.randn(bt, t_len, n, generator=g).to(device)
+    dy = torch.randn(bt, t_len, d, generator=g).to(device)
+
+    def fused():
+        leaves = [t.detach().requires_grad_(True) for t in (x, logit, a, b_in, c_in)]
+        y = selective_scan_proj(*leaves, 0.001, 0.1, impl="cuda", chunk=kk)
+        return torch.autograd.grad(y, leaves, grad_outputs=dy)
+
+    def unfused():
+        leaves = [t.detach().requires_grad_(True) for t in (x, logit, a, b_in, c_in)]
+        dt, aneg = proj_ref(leaves[1], leaves[2], 0.001, 0.1)
+        y = selective_scan(leaves[0], dt, aneg, leaves[3], leaves[4], impl="cuda", chunk=kk)
+        return torch.autograd.grad(y, leaves, grad_outputs=dy)
+
+    out = {}
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        k = 20
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        out[f"{name}_ms"] = s0.elapsed_time(s1) / k
+    out["value"] = bt * t_len * d / (out["fused_ms"] * 1e-3)
+    out["unit"] = UNIT
+    out["workload"] = (f"fwd+bwd with dt = 0.001 + 0.099*sigmoid(logit), Aneg = softplus(A) "
+                       f"at B{bt} T{t_len} D{d} N{n} K{kk}: fused in the kernels vs PyTorch ops "
+                       "before the scan (autograd through both)")
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -617,6 +668,7 @@ def main():
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step timing")
+    ap.add_argument("--no-proj", action="store_true", help="skip the fused-prologue timing")
     ap.add_argument("--shard", choices=("batch", "channel"), default=None,
                     help="multi-GPU split (default: channel for c4, batch otherwise)")
     ap.add_argument("--no-stride64", action="store_true",

@@ -53,7 +53,7 @@ extern "C" {
                                       (reported by mms_device_status)                    */
 
 /* Version of the ABI in this header (major * 100 + minor). */
-#define MMS_ABI_VERSION 101
+#define MMS_ABI_VERSION 102
 int mms_abi_version(void);
 
 /* Human-readable text for an MMS_* status. Never NULL. */
@@ -69,6 +69,20 @@ int mms_fwd(const float *x, const float *dt, const float *aneg,
             const float *B, const float *C,
             float *y, float *ckpt,
             int Bt, int T, int D, int N, int K, void *stream);
+
+/*
+ * Forward scan with the model's _proj prologue fused in (reference
+ * mamba_metal/model.py:191-201, which computes these with PyTorch ops before
+ * calling the scan):
+ *     dt   = dt_min + (dt_max - dt_min) * sigmoid(dt_logit)      (Bt, T, D)
+ *     Aneg = softplus(a_param)                                    (D, N)
+ * Otherwise exactly mms_fwd(). Needs finite dt_min < dt_max.
+ * No counterpart in the reference.
+ */
+int mms_fwd_proj(const float *x, const float *dt_logit, const float *a_param,
+                 const float *B, const float *C, float dt_min, float dt_max,
+                 float *y, float *ckpt,
+                 int Bt, int T, int D, int N, int K, void *stream);
 
 /*
  * Bytes of device workspace mms_bwd() needs for this shape.
@@ -90,6 +104,19 @@ int mms_bwd(const float *x, const float *dt, const float *aneg,
             float *dx, float *ddt, float *daneg, float *dB, float *dC,
             void *workspace, size_t workspace_bytes,
             int Bt, int T, int D, int N, int K, void *stream);
+
+/*
+ * Backward of mms_fwd_proj(): gradients with respect to x, dt_logit, a_param,
+ * B and C (d_dt_logit = ddt * dsigmoid, d_a_param = dAneg * sigmoid(a_param)).
+ * Same workspace as mms_bwd() (mms_bwd_workspace_size), ckpt from
+ * mms_fwd_proj(). No counterpart in the reference.
+ */
+int mms_bwd_proj(const float *x, const float *dt_logit, const float *a_param,
+                 const float *B, const float *C, const float *dy, const float *ckpt,
+                 float dt_min, float dt_max,
+                 float *dx, float *d_dt_logit, float *d_a_param, float *dB, float *dC,
+                 void *workspace, size_t workspace_bytes,
+                 int Bt, int T, int D, int N, int K, void *stream);
 
 /*
  * Backward scan that allocates nothing, for callers that cannot allocate

@@ -22,6 +22,50 @@ int check_shape(int Bt, int T, int D, int N, int K)
     return MMS_OK;
 }
 
+int fwd_impl(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
+             float *y, float *ckpt, int Bt, int T, int D, int N, int K, void *stream,
+             mms::Proj proj)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if (!x || !dt || !aneg || !B || !C || !y || !ckpt) return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
+        return MMS_ERR_MISALIGNED;
+    mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, proj};
+    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
+}
+
+int bwd_impl(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
+             const float *dy, const float *ckpt, float *dx, float *ddt, float *daneg, float *dB,
+             float *dC, void *workspace, size_t workspace_bytes, int Bt, int T, int D, int N,
+             int K, void *stream, mms::Proj proj)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if (!x || !dt || !aneg || !B || !C || !dy || !ckpt || !dx || !ddt || !daneg || !dB || !dC)
+        return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(daneg, 16) || !aligned(dB, 16) || !aligned(dC, 16) || !aligned(x, 4) ||
+        !aligned(dt, 4) || !aligned(dy, 4) || !aligned(dx, 4) || !aligned(ddt, 4))
+        return MMS_ERR_MISALIGNED;
+    const size_t need = mms::bwd_workspace_layout(Bt, T, D, N, K).total;
+    if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
+    mms::BwdArgs a{x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace,
+                   Bt, T, D, N, K, proj};
+    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
+}
+
+// dt = dt_min + (dt_max - dt_min) * sigmoid(logit) needs finite bounds in order.
+bool proj_ok(float dt_min, float dt_max)
+{
+    return dt_min == dt_min && dt_max == dt_max && dt_min > -3.0e38f && dt_max < 3.0e38f &&
+           dt_max > dt_min;
+}
+
 }  // namespace
 
 extern "C" {
@@ -48,15 +92,16 @@ const char *mms_status_string(int status)
 int mms_fwd(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
             float *y, float *ckpt, int Bt, int T, int D, int N, int K, void *stream)
 {
-    int rc = check_shape(Bt, T, D, N, K);
-    if (rc) return rc;
-    if (!x || !dt || !aneg || !B || !C || !y || !ckpt) return MMS_ERR_INVALID_ARG;
-    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
-        !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
-        return MMS_ERR_MISALIGNED;
-    mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K};
-    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return fwd_impl(x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f});
+}
+
+int mms_fwd_proj(const float *x, const float *dt_logit, const float *a_param, const float *B,
+                 const float *C, float dt_min, float dt_max, float *y, float *ckpt, int Bt, int T,
+                 int D, int N, int K, void *stream)
+{
+    if (!proj_ok(dt_min, dt_max)) return MMS_ERR_INVALID_ARG;
+    return fwd_impl(x, dt_logit, a_param, B, C, y, ckpt, Bt, T, D, N, K, stream,
+                    mms::Proj{1, dt_min, dt_max - dt_min});
 }
 
 size_t mms_bwd_workspace_size(int Bt, int T, int D, int N, int K)
@@ -70,20 +115,20 @@ int mms_bwd(const float *x, const float *dt, const float *aneg, const float *B, 
             float *dC, void *workspace, size_t workspace_bytes, int Bt, int T, int D, int N, int K,
             void *stream)
 {
-    int rc = check_shape(Bt, T, D, N, K);
-    if (rc) return rc;
-    if (!x || !dt || !aneg || !B || !C || !dy || !ckpt || !dx || !ddt || !daneg || !dB || !dC)
-        return MMS_ERR_INVALID_ARG;
-    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
-        !aligned(daneg, 16) || !aligned(dB, 16) || !aligned(dC, 16) || !aligned(x, 4) ||
-        !aligned(dt, 4) || !aligned(dy, 4) || !aligned(dx, 4) || !aligned(ddt, 4))
-        return MMS_ERR_MISALIGNED;
-    const size_t need = mms::bwd_workspace_layout(Bt, T, D, N, K).total;
-    if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
-    if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
-    mms::BwdArgs a{x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace, Bt, T, D, N, K};
-    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return bwd_impl(x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace, workspace_bytes,
+                    Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f});
+}
+
+int mms_bwd_proj(const float *x, const float *dt_logit, const float *a_param, const float *B,
+                 const float *C, const float *dy, const float *ckpt, float dt_min, float dt_max,
+                 float *dx, float *d_dt_logit, float *d_a_param, float *dB, float *dC,
+                 void *workspace, size_t workspace_bytes, int Bt, int T, int D, int N, int K,
+                 void *stream)
+{
+    if (!proj_ok(dt_min, dt_max)) return MMS_ERR_INVALID_ARG;
+    return bwd_impl(x, dt_logit, a_param, B, C, dy, ckpt, dx, d_dt_logit, d_a_param, dB, dC,
+                    workspace, workspace_bytes, Bt, T, D, N, K, stream,
+                    mms::Proj{1, dt_min, dt_max - dt_min});
 }
 
 int mms_step(const float *x, const float *dt, const float *aneg, const float *B, const float *C,

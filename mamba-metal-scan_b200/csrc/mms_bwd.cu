@@ -146,7 +146,7 @@ __device__ __forceinline__ float2 shfl2(float2 v, int m) {
 
 // Rewrite a natural tile into the compute layouts (see the file comment).
 template <int G>
-__device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int tid)
+__device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int tid, const Proj &pj)
 {
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, NROWF = S::NROWF, QF = S::QF, PF = S::PF;
@@ -155,8 +155,11 @@ __device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int t
         const int a = e / (NQ * DPB), rem = e % (NQ * DPB);
         const int q = rem / DPB, cc = rem % DPB;
         const float *src = nat + (4 * q) * NROWF + a * DPB + cc;
-        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) =
-            make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+        float4 v4 = make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+        if (pj.on && a == 1)
+            v4 = make_float4(fmaf(pj.range, sigmoid_fast(v4.x), pj.lo), fmaf(pj.range, sigmoid_fast(v4.y), pj.lo),
+                             fmaf(pj.range, sigmoid_fast(v4.z), pj.lo), fmaf(pj.range, sigmoid_fast(v4.w), pj.lo));
+        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) = v4;
     }
     constexpr int NQ4 = NPAD / 4;
     for (int e = tid; e < 2 * GRP * S::NPERM * NQ4; e += BWD_THREADS) {
@@ -221,7 +224,7 @@ struct Lane {
     bool n_writer;       // ... and stores it
     float2 an2[2];                                  // Aneg * log2(e) in lane state order
 
-    __device__ Lane(const float *aneg, int D, int N) {
+    __device__ Lane(const float *aneg, int D, int N, const Proj &pj) {
         tid = threadIdx.x;
         lane = tid & 31;
         warp = tid >> 5;
@@ -247,8 +250,14 @@ struct Lane {
         an2[1] = f2(0.f, 0.f);
         if (act) {
             const float *ap = aneg + (size_t)d * N + 4 * g;
-            an2[0] = f2(__ldg(ap + (0 ^ tau)) * MMS_LOG2E, __ldg(ap + (1 ^ tau)) * MMS_LOG2E);
-            an2[1] = f2(__ldg(ap + (2 ^ tau)) * MMS_LOG2E, __ldg(ap + (3 ^ tau)) * MMS_LOG2E);
+            float a[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                a[r] = __ldg(ap + (r ^ tau));
+                if (pj.on) a[r] = softplus(a[r]);
+            }
+            an2[0] = f2(a[0] * MMS_LOG2E, a[1] * MMS_LOG2E);
+            an2[1] = f2(a[2] * MMS_LOG2E, a[3] * MMS_LOG2E);
         }
     }
     // The 4 states of channel d, group g, in lane order, from a (D, N) plane.
@@ -281,7 +290,8 @@ struct Adjoint {
 template <int G, bool FULL>
 __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&hb)[2],
                                            const Lane<G> &L, Adjoint &A, int nv,
-                                           float *dxo, float *ddto, int D, float *sd)
+                                           float *dxo, float *ddto, int D, float *sd,
+                                           const Proj &pj)
 {
     float *outp = L.n_ddt ? ddto : dxo;
     using S = BwdShape<G>;
@@ -354,8 +364,11 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
                 if constexpr (G > 1) {
                     int fn;
                     transposed_reduce<2, G / 2, 1>(vn, L.lane, fn);
+                    // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
+                    if (pj.on && L.n_ddt) vn[0] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
                     if (L.n_writer) outp[(size_t)i * D] = vn[0];
                 } else if (L.n_writer) {
+                    if (pj.on) vn[1] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
                     dxo[(size_t)i * D] = vn[0];
                     ddto[(size_t)i * D] = vn[1];
                 }
@@ -447,7 +460,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ ckpt, float *__restrict__ dx,
            float *__restrict__ ddt, float *__restrict__ part_bc,
            float *__restrict__ part_a, float *subck, const float *__restrict__ seg_e,
-           int T, int D, int N, int K, int nblk, int nsegk, int cps)
+           int T, int D, int N, int K, int nblk, int nsegk, int cps, Proj pj)
 {
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
@@ -457,7 +470,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     float *sd = der + DER_BUFS * S::DERF;                            // [2][GRP][WARPS][NV2]
     float4 *slots = reinterpret_cast<float4 *>(sd + 2 * S::SDF);     // [SLOTS][THREADS]
 
-    const Lane<G> L(aneg, D, N);
+    const Lane<G> L(aneg, D, N, pj);
     const int tid = L.tid;
     const int nchunk = (T + K - 1) / K;
     const size_t plane = (size_t)D * N;
@@ -484,7 +497,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     }
     cp_wait<NAT_BUFS - 1>();
     __syncthreads();
-    rewrite_tile<G>(nat, der, tid);
+    rewrite_tile<G>(nat, der, tid, pj);
 
     Adjoint A;
     init_adjoint<G>(A, L, seg_e, sg, nsg, D, N);
@@ -504,7 +517,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             nxt.advance();
             if (!nxt.done())
                 rewrite_tile<G>(nat + ((it + 1) % NAT_BUFS) * S::NATF,
-                                der + ((it + 1) % DER_BUFS) * S::DERF, tid);
+                                der + ((it + 1) % DER_BUFS) * S::DERF, tid, pj);
         }
         if (!pre.done()) {                            // item it+3 into item it's natural tile
             stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
@@ -568,8 +581,8 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         }
         float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
         float *sdb = sd + (nw & 1) * S::SDF;
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
-        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
         ++nw;
         pend_t0 = t0;
         pend_nv = nv;
@@ -591,7 +604,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ ckpt, float *__restrict__ dx,
               float *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
-              int T, int D, int N, int nblk, int cps)
+              int T, int D, int N, int nblk, int cps, Proj pj)
 {
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
@@ -601,7 +614,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     float *sd = der + DER_BUFS * S::DERF;               // [2][GRP][WARPS][NV2]
     float *cks = sd + 2 * S::SDF;                      // [NAT_BUFS][DPB][NPAD] entry states
 
-    const Lane<G> L(aneg, D, N);
+    const Lane<G> L(aneg, D, N, pj);
     const int tid = L.tid;
     const int nchunk = (T + GRP - 1) / GRP;
     const size_t plane = (size_t)D * N;
@@ -643,7 +656,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     }
     cp_wait<NAT_BUFS - 1>();
     __syncthreads();
-    rewrite_tile<G>(nat, der, tid);
+    rewrite_tile<G>(nat, der, tid, pj);
     float2 hnext[2];                                   // state entering the current group
     entry(hnext, 0);
 
@@ -660,7 +673,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const float2 hb[2] = {hnext[0], hnext[1]};
         if (c - 1 >= clo) {                            // group it+1: rewrite, take its entry state
             const int nb = (it + 1) % NAT_BUFS;
-            rewrite_tile<G>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid);
+            rewrite_tile<G>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid, pj);
             entry(hnext, nb);
         }
         if (c - NAT_BUFS >= clo) stage((it + NAT_BUFS) % NAT_BUFS, c - NAT_BUFS);
@@ -672,8 +685,8 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const int nv = min(GRP, T - t0);
         float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
         float *sdb = sd + (it & 1) * S::SDF;
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb);
-        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb);
+        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
+        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
     }
     cp_wait<0>();
     __syncthreads();
@@ -701,13 +714,15 @@ __global__ void reduce_bc_kernel(const float *__restrict__ part, float *__restri
 }
 
 // dAneg = sum over the (batch row, time segment) partials (fixed order).
+// With the prologue, the gradient of the raw A is dAneg * softplus'(A) = dAneg * sigmoid(A).
 __global__ void reduce_a_kernel(const float *__restrict__ part, float *__restrict__ daneg,
-                                int rows, size_t DN)
+                                int rows, size_t DN, const float *__restrict__ a_raw, int proj)
 {
     for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < DN;
          idx += (size_t)gridDim.x * blockDim.x) {
         float s = 0.f;
         for (int r = 0; r < rows; ++r) s += part[(size_t)r * DN + idx];
+        if (proj) s *= 1.f / (1.f + expf(-a_raw[idx]));
         daneg[idx] = s;
     }
 }
@@ -756,7 +771,7 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     if (sp.S > 1) {
         // local adjoint carries of segments 1..S-1, then the chain (last to first)
         SegLocalArgs la{a.dy, a.dt, a.aneg, a.C, seg_e, seg_p, a.Bt, a.T, a.D, a.N,
-                        sp.cps * a.K, 1, sp.S - 1, sp.S, 1, 0, 0};
+                        sp.cps * a.K, 1, sp.S - 1, sp.S, 1, 0, 0, a.proj};
         if ((e = launch_seg_local(la, true, stream)) != cudaSuccess) return e;
         if ((e = launch_seg_combine_bwd(seg_e, seg_p, a.Bt, sp.S, (size_t)a.D * a.N, stream)) !=
             cudaSuccess)
@@ -771,14 +786,14 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
         if (e != cudaSuccess) return e;
         bwd_kernel_k8<G, VEC><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e,
-            a.T, a.D, a.N, w.nblk, sp.cps);
+            a.T, a.D, a.N, w.nblk, sp.cps, a.proj);
     } else {
         e = cudaFuncSetAttribute(bwd_kernel<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM);
         if (e != cudaSuccess) return e;
         bwd_kernel<G, VEC><<<grid, BWD_THREADS, S::SMEM, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck, seg_e,
-            a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps);
+            a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps, a.proj);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t nbc = (size_t)a.Bt * a.T * 2 * a.N;
@@ -787,7 +802,7 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const size_t dn = (size_t)a.D * a.N;
     const int ra = (int)((dn + 255) / 256 < 148 * 16 ? (dn + 255) / 256 : 148 * 16);
-    reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt * sp.S, dn);
+    reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt * sp.S, dn, a.aneg, a.proj.on);
     return cudaGetLastError();
 }
 

@@ -96,7 +96,7 @@ __device__ __forceinline__ float2 shfl2x(float2 v, int m) {
 // The rewrite: staged tile -> 4-step runs and permuted B/C. TMA selects the
 // stage layout: array-major (TMA) or one interleaved row per step (cp.async).
 template <bool TMA>
-__device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid)
+__device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid, const Proj &pj)
 {
     constexpr int DPB = W8_DPB, NROWF = W8Shape::NROWF, QF = W8Shape::QF, PF = W8Shape::PF;
     constexpr int AROW = TMA ? DPB : NROWF;                      // step stride, channel arrays
@@ -108,8 +108,11 @@ __device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid
     for (int e = tid; e < 3 * 2 * DPB; e += W8_THREADS) {
         const int a = e / (2 * DPB), q = (e / DPB) & 1, cc = e % DPB;
         const float *src = nat + (4 * q) * AROW + a * AOFF + cc;
-        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) =
-            make_float4(src[0], src[AROW], src[2 * AROW], src[3 * AROW]);
+        float4 v4 = make_float4(src[0], src[AROW], src[2 * AROW], src[3 * AROW]);
+        if (pj.on && a == 1)        // prologue: dt from its logit
+            v4 = make_float4(fmaf(pj.range, sigmoid_fast(v4.x), pj.lo), fmaf(pj.range, sigmoid_fast(v4.y), pj.lo),
+                             fmaf(pj.range, sigmoid_fast(v4.z), pj.lo), fmaf(pj.range, sigmoid_fast(v4.w), pj.lo));
+        *reinterpret_cast<float4 *>(der + a * QF + (q * DPB + cc) * 4) = v4;
     }
     // B, C: der[3QF + a*PF + (i*8 + tau)*16 + 8h + r] = arr_a[i][8h + (r ^ tau)]
     for (int e = tid; e < 2 * W8_CH * 8 * 4; e += W8_THREADS) {
@@ -129,7 +132,7 @@ struct W8Lane {
     int tid, lane, warp, h, c, d0, d, b, tau, kbit;
     bool dval;
     float2 an2[4];                 // Aneg * log2(e), lane state order
-    __device__ W8Lane(const float *aneg, int D, int N) {
+    __device__ W8Lane(const float *aneg, int D, int N, const Proj &pj) {
         tid = threadIdx.x;
         lane = tid & 31;
         warp = tid >> 5;
@@ -145,8 +148,14 @@ struct W8Lane {
         for (int p = 0; p < 4; ++p) {
             float v0 = 0.f, v1 = 0.f;
             const int s0 = 8 * h + ((2 * p) ^ tau), s1 = 8 * h + ((2 * p + 1) ^ tau);
-            if (dval && s0 < N) v0 = __ldg(aneg + (size_t)d * N + s0) * MMS_LOG2E;
-            if (dval && s1 < N) v1 = __ldg(aneg + (size_t)d * N + s1) * MMS_LOG2E;
+            if (dval && s0 < N) v0 = __ldg(aneg + (size_t)d * N + s0);
+            if (dval && s1 < N) v1 = __ldg(aneg + (size_t)d * N + s1);
+            if (pj.on) {
+                v0 = dval && s0 < N ? softplus(v0) : 0.f;
+                v1 = dval && s1 < N ? softplus(v1) : 0.f;
+            }
+            v0 *= MMS_LOG2E;
+            v1 *= MMS_LOG2E;
             an2[p] = f2(v0, v1);
         }
     }
@@ -207,7 +216,8 @@ struct W8Adj {
 // Rebuild quad q from hb, then walk it backwards.
 template <bool FULL>
 __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], const W8Lane &L,
-                                        W8Adj &A, int q, int nv, float *outq, int D, float *sd)
+                                        W8Adj &A, int q, int nv, float *outq, int D, float *sd,
+                                        const Proj &pj)
 {
     float2 hv[4][4];
     {
@@ -257,6 +267,8 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
             const float v0 = dtv * s1, v1 = fmaf(xv, s1, -W8_LN2 * s2);
             float keep = L.h ? v1 : v0;
             keep += __shfl_xor_sync(0xffffffffu, L.h ? v0 : v1, 1);
+            // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
+            if (pj.on && L.h) keep *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
             if (L.dval) outq[(size_t)k * D] = keep;
         }
         // dB|dC over the warp's 16 channels
@@ -284,7 +296,7 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
 // thread issues 6 loads per chunk; out-of-range steps, channels, states and
 // the chunk-0 entry state arrive as zeros) and complete on per-stage
 // mbarriers.
-template <bool VEC, bool TMA>
+template <bool VEC, bool TMA, bool PROJ>
 __global__ void __launch_bounds__(W8_THREADS, MMS_BWD_W8_MINB)
 bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
@@ -292,8 +304,12 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ ckpt, float *__restrict__ dx,
               float *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
-              int T, int D, int N, int nblk, int cps, const __grid_constant__ W8Maps maps)
+              int T, int D, int N, int nblk, int cps, const __grid_constant__ W8Maps maps,
+              Proj pj_in)
 {
+    // the prologue is compiled in only where it is used
+    Proj pj = pj_in;
+    pj.on = PROJ;
     constexpr int DPB = W8_DPB;
     extern __shared__ __align__(128) float smem[];
     float *nat = smem;                                     // [W8_NAT][STAGEF]
@@ -301,7 +317,7 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
     float *sd = der + W8Shape::DERF;                       // [CH][WARPS][32]
     const uint32_t bars = smem_u32(sd + W8Shape::SDF);     // TMA: W8_NAT stage barriers
 
-    const W8Lane L(aneg, D, N);
+    const W8Lane L(aneg, D, N, pj);
     const int tid = L.tid;
     const int nchunk = (T + W8_CH - 1) / W8_CH;
     const size_t plane = (size_t)D * N;
@@ -381,7 +397,7 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
             }
         }
         const float *st = nat + (it % W8_NAT) * W8Shape::STAGEF;
-        w8_rewrite<TMA>(st, der, tid);
+        w8_rewrite<TMA>(st, der, tid, pj);
         float2 hA[4];
         L.load8(hA, st + (TMA ? W8Shape::T_CK : W8Shape::NATF) + L.c * 16, 16);
         if (c - 2 >= clo) {
@@ -400,11 +416,11 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
         if (nv > 4) {
             float2 h4[4] = {hA[0], hA[1], hA[2], hA[3]};
             w8_advance(h4, L, v, 0);
-            if (nv == W8_CH) w8_walk<true>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd);
-            else w8_walk<false>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd);
-            w8_walk<true>(v, hA, L, A, 0, nv, outb, D, sd);
+            if (nv == W8_CH) w8_walk<true>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
+            else w8_walk<false>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
+            w8_walk<true>(v, hA, L, A, 0, nv, outb, D, sd, pj);
         } else {
-            w8_walk<false>(v, hA, L, A, 0, nv, outb, D, sd);
+            w8_walk<false>(v, hA, L, A, 0, nv, outb, D, sd, pj);
         }
     }
     cp_wait<0>();
@@ -457,19 +473,27 @@ bool build_maps(const BwdArgs &a, W8Maps *m)
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
+template <bool VEC, bool TMA, bool PROJ>
+cudaError_t launch_w8p(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                       int nblk, SegPlan sp, const W8Maps &maps, cudaStream_t stream)
+{
+    const size_t smem = TMA ? W8Shape::SMEM_TMA : W8Shape::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(bwd_kernel_w8<VEC, TMA, PROJ>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
+    bwd_kernel_w8<VEC, TMA, PROJ><<<grid, W8_THREADS, smem, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e, a.T, a.D,
+        a.N, nblk, sp.cps, maps, a.proj);
+    return cudaGetLastError();
+}
+
 template <bool VEC, bool TMA>
 cudaError_t launch_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                       int nblk, SegPlan sp, const W8Maps &maps, cudaStream_t stream)
 {
-    const size_t smem = TMA ? W8Shape::SMEM_TMA : W8Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(bwd_kernel_w8<VEC, TMA>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
-    bwd_kernel_w8<VEC, TMA><<<grid, W8_THREADS, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e, a.T, a.D,
-        a.N, nblk, sp.cps, maps);
-    return cudaGetLastError();
+    return a.proj.on ? launch_w8p<VEC, TMA, true>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream)
+                     : launch_w8p<VEC, TMA, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
 }
 
 }  // namespace

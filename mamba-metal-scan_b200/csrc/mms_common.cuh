@@ -25,6 +25,16 @@ __device__ __forceinline__ float ex2_fresh(float x) {
     return y;
 }
 
+// sigmoid(z) = 1 / (1 + 2^(-z*log2 e)); saturates to 0 / 1 for large |z|.
+__device__ __forceinline__ float sigmoid_fast(float z) {
+    return __frcp_rn(1.f + ex2(-z * MMS_LOG2E));
+}
+
+// softplus(a) = log(1 + e^a), = a once e^a dwarfs 1 in fp32.
+__device__ __forceinline__ float softplus(float a) {
+    return a > 20.f ? a : log1pf(expf(a));
+}
+
 __device__ __forceinline__ float4 ld4(const float *p) {
     return __ldg(reinterpret_cast<const float4 *>(p));
 }

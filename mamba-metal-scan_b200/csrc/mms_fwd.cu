@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 2)
 fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
            const float *__restrict__ Cm, float *__restrict__ y,
-           float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps)
+           float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps, Proj pj)
 {
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
@@ -67,7 +67,8 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
     // -Aneg * log2(e) as two packed pairs: dA = 2^(dt * nan2).
     float2 nan2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
     if (act) {
-        const float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
+        float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
+        if (pj.on) a4 = make_float4(softplus(a4.x), softplus(a4.y), softplus(a4.z), softplus(a4.w));
         nan2[0] = f2(-a4.x * MMS_LOG2E, -a4.y * MMS_LOG2E);
         nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
@@ -117,7 +118,8 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
             const float *row = tile + j * ROWF;
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
             const float xv = row[c];
-            const float dtv = row[DPB + c];
+            float dtv = row[DPB + c];
+            if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
             const float4 Bv = *reinterpret_cast<const float4 *>(row + 2 * DPB + 4 * g);
             const float4 Cv = *reinterpret_cast<const float4 *>(row + 2 * DPB + NPAD + 4 * g);
             const float bx = dtv * xv;
@@ -207,14 +209,16 @@ __device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
 // on per-stage mbarriers, in an array-major layout [x TTxDPB][dt TTxDPB]
 // [B TTx16][C TTx16]; out-of-range steps, channels and states load as zeros,
 // like the cp.async path's zero fill.
-template <bool VEC, bool BULK, bool TMA>
+template <bool VEC, bool BULK, bool TMA, bool PROJ>
 __global__ void __launch_bounds__(S16_DPB, 2)
 fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, float *__restrict__ y,
                float *__restrict__ ckpt, int T, int D, int N, int K,
-               const __grid_constant__ FwdMaps maps)
+               const __grid_constant__ FwdMaps maps, Proj pj_in)
 {
+    Proj pj = pj_in;                                       // the prologue only where used
+    pj.on = PROJ;
     constexpr int DPB = S16Shape::DPB, ROWF = S16Shape::ROWF, TT = S16_TT;
     // where step j of a tile keeps x, dt, B, C (floats from the tile start)
     constexpr int XROW = TMA ? DPB : ROWF, XOFF = 0;
@@ -241,7 +245,8 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     for (int p = 0; p < 8; ++p) {
         float a0 = 0.f, a1 = 0.f;
         if (dval && 2 * p < N) {
-            const float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + 2 * p);
+            float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + 2 * p);
+            if (pj.on) v = f2(softplus(v.x), softplus(v.y));
             a0 = -v.x * MMS_LOG2E;
             a1 = -v.y * MMS_LOG2E;
         }
@@ -329,7 +334,8 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         for (int j = 0; j < TT; ++j) {
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
             const float xv = tile[XOFF + j * XROW + tid];
-            const float dtv = tile[DOFF + j * XROW + tid];
+            float dtv = tile[DOFF + j * XROW + tid];
+            if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
             const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW);
             const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
             const float bx = dtv * xv;
@@ -383,17 +389,24 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     }
 }
 
-template <bool VEC, bool BULK, bool TMA>
-static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
+template <bool VEC, bool BULK, bool TMA, bool PROJ>
+static cudaError_t launch_fwd_s16_p(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
 {
     const size_t smem = TMA ? S16Shape::SMEM_TMA : BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA>,
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA, PROJ>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt);
-    fwd_kernel_s16<VEC, BULK, TMA><<<grid, S16_DPB, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, maps);
+    fwd_kernel_s16<VEC, BULK, TMA, PROJ><<<grid, S16_DPB, smem, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, maps, a.proj);
     return cudaGetLastError();
+}
+
+template <bool VEC, bool BULK, bool TMA>
+static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
+{
+    return a.proj.on ? launch_fwd_s16_p<VEC, BULK, TMA, true>(a, maps, stream)
+                     : launch_fwd_s16_p<VEC, BULK, TMA, false>(a, maps, stream);
 }
 
 #ifndef MMS_FWD_BULK
@@ -455,7 +468,7 @@ static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
     if (sp.S > 1) {
         // local end states and decay products of segments 0..S-2, then the chain
         SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, L, 0,
-                        sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2};
+                        sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj};
         if ((e = launch_seg_local(la, false, stream)) != cudaSuccess) return e;
         if ((e = launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N,
                                         stream)) != cudaSuccess)
@@ -463,7 +476,7 @@ static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
     }
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt, sp.S);
     fwd_kernel<G, VEC><<<grid, FWD_THREADS, S::SMEM, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps);
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps, a.proj);
     return cudaGetLastError();
 }
 

@@ -7,10 +7,21 @@
 
 namespace mms {
 
+// The fused _proj prologue (reference mamba_metal/model.py:191-201): when
+// `on`, the dt argument holds logits z and the aneg argument holds the raw
+// parameter A, and the kernels use
+//     dt = lo + range * sigmoid(z),     Aneg = softplus(A),
+// returning gradients with respect to z and A.
+struct Proj {
+    int on;
+    float lo, range;
+};
+
 struct FwdArgs {
     const float *x, *dt, *aneg, *B, *C;
     float *y, *ckpt;
     int Bt, T, D, N, K;
+    Proj proj;
 };
 
 struct BwdArgs {
@@ -18,6 +29,7 @@ struct BwdArgs {
     float *dx, *ddt, *daneg, *dB, *dC;
     void *workspace;
     int Bt, T, D, N, K;
+    Proj proj;
 };
 
 struct StepArgs {
@@ -104,6 +116,7 @@ struct SegLocalArgs {
     const float *u, *dt, *aneg, *row;
     float *vout, *pout;
     int Bt, T, D, N, L, s_first, nseg, bplanes, splanes, voff, poff;
+    Proj proj;
 };
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream);
 

@@ -51,7 +51,7 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
                  const float *__restrict__ aneg, const float *__restrict__ row,
                  float *__restrict__ vout, float *__restrict__ pout,
                  int T, int D, int N, int L, int s_first, int bplanes, int splanes,
-                 int voff, int poff)
+                 int voff, int poff, Proj pj)
 {
     using S = SegLocalShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, ROWF = S::ROWF, TT = SEGL_TT;
@@ -70,7 +70,8 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
 
     float2 nan2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
     if (act) {
-        const float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
+        float4 a4 = ld4(aneg + (size_t)d * N + 4 * g);
+        if (pj.on) a4 = make_float4(softplus(a4.x), softplus(a4.y), softplus(a4.z), softplus(a4.w));
         nan2[0] = f2(-a4.x * MMS_LOG2E, -a4.y * MMS_LOG2E);
         nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
@@ -100,12 +101,16 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
         if (kn < ntiles) stage(kn % SEGL_STAGES, kn);
         cp_commit();
         const float *tile = smem + (k % SEGL_STAGES) * TT * ROWF;
+        const int tk = tstart(k);
 #pragma unroll
         for (int jj = 0; jj < TT; ++jj) {
             // rows past the segment's end were staged as zeros: dA = 1, no input
+            // (with the prologue, dt = 0 must be kept there rather than mapped)
             const int j = BWD ? TT - 1 - jj : jj;
             const float *r = tile + j * ROWF;
-            const float uv = r[c], dtv = r[DPB + c];
+            const float uv = r[c];
+            float dtv = r[DPB + c];
+            if (pj.on) dtv = tk + j < te ? fmaf(pj.range, sigmoid_fast(dtv), pj.lo) : 0.f;
             const float4 R = *reinterpret_cast<const float4 *>(r + 2 * DPB + 4 * g);
             const float2 dt2 = f2(dtv, dtv);
             const float2 a0 = ex2x2(mul2(dt2, nan2[0])), a1 = ex2x2(mul2(dt2, nan2[1]));
@@ -184,7 +189,7 @@ static cudaError_t launch_local_gv(const SegLocalArgs &a, cudaStream_t stream)
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.nseg, a.Bt);
     seg_local_kernel<G, BWD, VEC><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
         a.u, a.dt, a.aneg, a.row, a.vout, a.pout, a.T, a.D, a.N, a.L, a.s_first, a.bplanes,
-        a.splanes, a.voff, a.poff);
+        a.splanes, a.voff, a.poff, a.proj);
     return cudaGetLastError();
 }
 

@@ -1,13 +1,15 @@
 """Fused selective-scan kernels for Mamba on NVIDIA B200 (sm_100a).
 
 Drop-in for Anamaya1729/mamba-metal-scan's `mamba_metal` package: the same
-exports, plus `selective_scan_cuda` and the one-token decode step
-`selective_scan_step`.
+exports, plus `selective_scan_cuda`, the one-token decode step
+`selective_scan_step` and `selective_scan_proj` (the scan with the model's dt
+and Aneg prologue fused into the kernels).
 """
 from mamba_metal.model import MambaConfig, TinyMamba
 from mamba_metal.scan import (selective_scan, selective_scan_cuda, selective_scan_metal,
-                              selective_scan_ref, selective_scan_step, selective_scan_step_ref)
+                              selective_scan_proj, selective_scan_ref, selective_scan_step,
+                              selective_scan_step_ref)
 
 __all__ = ["MambaConfig", "TinyMamba", "selective_scan", "selective_scan_cuda",
-           "selective_scan_metal", "selective_scan_ref", "selective_scan_step",
-           "selective_scan_step_ref"]
+           "selective_scan_metal", "selective_scan_proj", "selective_scan_ref",
+           "selective_scan_step", "selective_scan_step_ref"]

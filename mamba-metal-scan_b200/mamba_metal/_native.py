@@ -36,6 +36,9 @@ SIGNATURES = {
     "mms_bwd_noalloc": ([_P] * 12 + [_I] * 5 + [_P], _I),
     "mms_step": ([_P] * 7 + [_I] * 3 + [_P], _I),
     "mms_device_status": ([], _I),
+    "mms_fwd_proj": ([_P] * 5 + [ctypes.c_float] * 2 + [_P] * 2 + [_I] * 5 + [_P], _I),
+    "mms_bwd_proj": ([_P] * 7 + [ctypes.c_float] * 2 + [_P] * 6 + [ctypes.c_size_t] + [_I] * 5
+                     + [_P], _I),
 }
 
 _lib = None
@@ -82,17 +85,26 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def fwd(x, dt, aneg, b_in, c_in, chunk: int):
-    """y (B,T,D) and ckpt (B, ceil(T/chunk), D, N) on the current stream."""
+def fwd(x, dt, aneg, b_in, c_in, chunk: int, proj=None):
+    """y (B,T,D) and ckpt (B, ceil(T/chunk), D, N) on the current stream.
+
+    proj = (dt_min, dt_max): dt holds logits and aneg the raw A of the fused
+    prologue (mms_fwd_proj)."""
     lib = load()
     bt, t_len, d = x.shape
     n = aneg.shape[1]
     nchunk = (t_len + chunk - 1) // chunk
     y = torch.empty(bt, t_len, d, device=x.device, dtype=torch.float32)
     ckpt = torch.empty(bt, nchunk, d, n, device=x.device, dtype=torch.float32)
-    rc = lib.mms_fwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(y), _ptr(ckpt),
-                     bt, t_len, d, n, chunk, _stream(x.device))
-    _check(rc, "mms_fwd")
+    if proj is None:
+        rc = lib.mms_fwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(y),
+                         _ptr(ckpt), bt, t_len, d, n, chunk, _stream(x.device))
+        _check(rc, "mms_fwd")
+    else:
+        rc = lib.mms_fwd_proj(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in),
+                              float(proj[0]), float(proj[1]), _ptr(y), _ptr(ckpt),
+                              bt, t_len, d, n, chunk, _stream(x.device))
+        _check(rc, "mms_fwd_proj")
     return y, ckpt
 
 
@@ -100,8 +112,9 @@ def bwd_workspace_size(bt: int, t_len: int, d: int, n: int, chunk: int) -> int:
     return int(load().mms_bwd_workspace_size(bt, t_len, d, n, chunk))
 
 
-def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None):
-    """(dx, ddt, dAneg, dB, dC) on the current stream."""
+def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None, proj=None):
+    """(dx, ddt, dAneg, dB, dC) on the current stream (with proj: the
+    gradients of the logits and of the raw A in place of ddt and dAneg)."""
     lib = load()
     bt, t_len, d = x.shape
     n = aneg.shape[1]
@@ -113,11 +126,19 @@ def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None):
     ws_bytes = bwd_workspace_size(bt, t_len, d, n, chunk)
     if workspace is None or workspace.numel() < ws_bytes:
         workspace = torch.empty(max(ws_bytes, 1), device=x.device, dtype=torch.uint8)
-    rc = lib.mms_bwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(dy), _ptr(ckpt),
-                     _ptr(dx), _ptr(ddt), _ptr(daneg), _ptr(db), _ptr(dc),
-                     _ptr(workspace), workspace.numel(),
-                     bt, t_len, d, n, chunk, _stream(x.device))
-    _check(rc, "mms_bwd")
+    if proj is None:
+        rc = lib.mms_bwd(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(dy),
+                         _ptr(ckpt), _ptr(dx), _ptr(ddt), _ptr(daneg), _ptr(db), _ptr(dc),
+                         _ptr(workspace), workspace.numel(),
+                         bt, t_len, d, n, chunk, _stream(x.device))
+        _check(rc, "mms_bwd")
+    else:
+        rc = lib.mms_bwd_proj(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(dy),
+                              _ptr(ckpt), float(proj[0]), float(proj[1]),
+                              _ptr(dx), _ptr(ddt), _ptr(daneg), _ptr(db), _ptr(dc),
+                              _ptr(workspace), workspace.numel(),
+                              bt, t_len, d, n, chunk, _stream(x.device))
+        _check(rc, "mms_bwd_proj")
     return dx, ddt, daneg, db, dc
 
 

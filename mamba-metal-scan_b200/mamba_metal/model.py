@@ -30,7 +30,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from mamba_metal.scan import selective_scan, selective_scan_step, selective_scan_step_ref
+from mamba_metal.scan import (selective_scan, selective_scan_proj, selective_scan_step,
+                              selective_scan_step_ref)
 
 
 @dataclass
@@ -45,6 +46,7 @@ class MambaConfig:
     d_inner: Optional[int] = None
     scan_chunk: int = 0       # time slice of the parallel_scan fallback; 0 = one pass
     scan_impl: str = "auto"   # 'auto' | 'cuda' | 'metal' | 'torch'
+    fuse_proj: bool = True    # CUDA scan computes dt and softplus(A) itself (selective_scan_proj)
     dt_min: float = 0.001
     dt_max: float = 0.1
     norm_eps: float = 1e-6
@@ -157,6 +159,7 @@ class MambaBlock(nn.Module):
         self.d_inner = d_inner
         self.scan_chunk = cfg.scan_chunk
         self.scan_impl = cfg.scan_impl
+        self.fuse_proj = cfg.fuse_proj
         self.dt_min, self.dt_max = cfg.dt_min, cfg.dt_max
         self.norm = RMSNorm(dm, cfg.norm_eps)
         self.in_proj = nn.Linear(dm, 2 * d_inner, bias=False)
@@ -184,6 +187,11 @@ class MambaBlock(nn.Module):
 
     def _scan(self, x, return_state=False):
         """y_t = sum_n C_tn h_tn; the fused scan when scan_impl allows it."""
+        if self.fuse_proj and x.is_cuda and self.scan_impl != "torch":
+            # dt and Aneg computed inside the kernels from dt_proj(x) and A
+            return selective_scan_proj(x, self.dt_proj(x), self.A, self.B_proj(x), self.C_proj(x),
+                                       self.dt_min, self.dt_max, impl=self.scan_impl,
+                                       return_state=return_state)
         dt, B_t, C_t, Aneg = self._proj(x)
         r = selective_scan(x, dt, Aneg, B_t, C_t, impl=self.scan_impl,
                            return_state=return_state)

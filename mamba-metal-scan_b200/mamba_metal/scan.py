@@ -194,6 +194,89 @@ def selective_scan(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
     return None
 
 
+# ------------------------------------------------- fused _proj prologue (f2)
+
+def proj_ref(dt_logit, a_param, dt_min: float, dt_max: float):
+    """(dt, Aneg) as the reference model computes them (model.py:191-201)."""
+    dt = dt_min + (dt_max - dt_min) * torch.sigmoid(dt_logit)
+    return dt, torch.nn.functional.softplus(a_param)
+
+
+class SelectiveScanProjCUDA(torch.autograd.Function):
+    """The scan with dt and Aneg computed from their raw parameters in the kernels.
+
+    forward(x, dt_logit, a_param, B, C, dt_min, dt_max, chunk, return_state):
+    dt = dt_min + (dt_max - dt_min)*sigmoid(dt_logit), Aneg = softplus(a_param),
+    then the scan; backward returns the gradients of x, dt_logit, a_param, B, C.
+    Saves (x, dt_logit, a_param, B, C, ckpt): no (B, T, D) dt tensor exists.
+    """
+
+    @staticmethod
+    def forward(ctx, x, dt_logit, a_param, b_in, c_in, dt_min, dt_max, chunk=SSM_CHUNK,
+                return_state=False):
+        _validate(x, dt_logit, a_param, b_in, c_in, "cuda")
+        chunk = int(chunk)
+        if chunk < 1:
+            raise ValueError(f"chunk (the checkpoint stride) must be >= 1; got {chunk}")
+        if not float(dt_max) > float(dt_min):
+            raise ValueError(f"need dt_min < dt_max; got {dt_min}, {dt_max}")
+        bt, t_len, d = x.shape
+        n = a_param.shape[1]
+        x, dt_logit = _aligned(x, 4), _aligned(dt_logit, 4)
+        a_param, b_in, c_in = _aligned(a_param, 16), _aligned(b_in, 16), _aligned(c_in, 16)
+        proj = (float(dt_min), float(dt_max))
+        with torch.cuda.device(x.device):
+            if bt == 0 or t_len == 0 or d == 0:
+                y, ckpt = x.new_zeros(bt, t_len, d), x.new_zeros(bt, 0, d, n)
+            else:
+                y, ckpt = _native.fwd(x, dt_logit, a_param, b_in, c_in, chunk, proj=proj)
+        ctx.save_for_backward(x, dt_logit, a_param, b_in, c_in, ckpt)
+        ctx.chunk, ctx.proj = chunk, proj
+        if return_state:
+            state = ckpt[:, -1].detach() if ckpt.shape[1] else x.new_zeros(bt, d, n)
+            return y, state
+        return y
+
+    @staticmethod
+    def backward(ctx, *grads):
+        dy = grads[0]
+        x, dt_logit, a_param, b_in, c_in, ckpt = ctx.saved_tensors
+        bt, t_len, d = x.shape
+        if dy is None or bt == 0 or t_len == 0 or d == 0:
+            return (torch.zeros_like(x), torch.zeros_like(dt_logit), torch.zeros_like(a_param),
+                    torch.zeros_like(b_in), torch.zeros_like(c_in), None, None, None, None)
+        dy = _aligned(dy.float(), 4)
+        with torch.cuda.device(x.device):
+            g = _native.bwd(x, dt_logit, a_param, b_in, c_in, dy, ckpt, ctx.chunk, proj=ctx.proj)
+        return (*g, None, None, None, None)
+
+
+def selective_scan_proj(x: torch.Tensor, dt_logit: torch.Tensor, a_param: torch.Tensor,
+                        b_in: torch.Tensor, c_in: torch.Tensor, dt_min: float, dt_max: float,
+                        impl: str = "auto", chunk: int = SSM_CHUNK, return_state: bool = False):
+    """selective_scan with the model's _proj prologue fused in.
+
+    Same as selective_scan(x, dt, Aneg, B, C) with
+    dt = dt_min + (dt_max - dt_min)*sigmoid(dt_logit) and Aneg = softplus(a_param),
+    differentiable with respect to dt_logit and a_param. On CUDA tensors the
+    kernels compute dt and Aneg themselves (mms_fwd_proj / mms_bwd_proj), so
+    the (B, T, D) dt tensor and its elementwise passes never exist; 'torch'
+    composes proj_ref with selective_scan_ref; off-CUDA 'auto' returns None.
+    """
+    if impl == "torch":
+        dt, aneg = proj_ref(dt_logit, a_param, dt_min, dt_max)
+        return selective_scan_ref(x, dt, aneg, b_in, c_in, return_state=return_state)
+    if impl not in _IMPLS:
+        raise ValueError(f"unknown scan_impl {impl!r}; want 'auto', 'cuda', 'metal' or 'torch'")
+    if x.is_cuda:
+        return SelectiveScanProjCUDA.apply(x, dt_logit, a_param, b_in, c_in, dt_min, dt_max,
+                                           chunk, return_state)
+    if impl in ("cuda", "metal"):
+        raise RuntimeError(f"scan_impl={impl!r} needs CUDA tensors (this build has no MPS/Metal "
+                           f"backend); got device {x.device.type!r}")
+    return None
+
+
 # ------------------------------------------------------------ decode (one token)
 
 def selective_scan_step_ref(x, dt, aneg, b_in, c_in, h):

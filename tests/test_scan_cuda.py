@@ -312,20 +312,20 @@ def test_end_to_end_torch_vs_cuda():
 def test_auto_selects_cuda_in_the_model():
     model = _tinymamba("auto")
     idx = torch.randint(0, 200, (2, 16), device=DEV)
-    from mamba_metal import scan as scan_mod
+    from mamba_metal import _native
     calls = []
-    orig = scan_mod.SelectiveScanCUDA.apply
+    orig = _native.fwd
 
-    def spy(*a):
+    def spy(*a, **k):
         calls.append(1)
-        return orig(*a)
+        return orig(*a, **k)
 
-    scan_mod.SelectiveScanCUDA.apply = spy
+    _native.fwd = spy
     try:
         model(idx, idx)
     finally:
-        scan_mod.SelectiveScanCUDA.apply = orig
-    assert len(calls) == 2
+        _native.fwd = orig
+    assert len(calls) == 2          # one CUDA forward per layer
 
 
 def test_recurrent_cache_matches_full_recomputation_on_cuda():
