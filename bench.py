@@ -21,6 +21,7 @@ Printed (rank 0): one JSON line with the contract keys plus
   train         TinyMamba config 2 (vocab 32768, d_model 640, 12 layers) tok/s
   decode        the one-token step kernel at the config-4 decode shape
   proj          the scan with the dt / softplus(A) prologue fused into the kernels
+  gate          the block's (y + D) * silu(z) epilogue, one kernel each way
   clocks        nvidia-smi samples taken during the timed region
 `--impl reference` times only the reference CPU path (rank 0) and prints its line.
 """
@@ -394,6 +395,7 @@ def run_native(args, shape):
         line["decode"] = run_decode(args, device, hbm_gbs)
     if not args.no_proj and world == 1:
         line["proj"] = run_proj(args, shape, device)
+        line["gate"] = run_gate(args, shape, device, hbm_gbs)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(shape, args.cpu_budget)
     if rank == 0:
@@ -654,6 +656,51 @@ def run_proj(args, shape, device):
     return out
 
 
+def run_gate(args, shape, device, hbm_gbs):
+    """Row f3: the block's (y + D_skip) * silu(z) epilogue as one kernel each
+    way (mms_gate_fwd / mms_gate_bwd) at the bench's (B, T, D), with z a
+    strided half of a (B, T, 2D) tensor as in the model; against the same
+    expression as PyTorch ops (forward + autograd backward)."""
+    from mamba_metal import _native
+    from mamba_metal.scan import gate_ref
+    bt, t_len, d, _, _ = shape
+    g = torch.Generator(device="cpu").manual_seed(5)
+    y = torch.randn(bt, t_len, d, generator=g).to(device)
+    zz = torch.randn(bt, t_len, 2 * d, generator=g).to(device)
+    z = zz[..., d:]
+    dskip = torch.randn(d, generator=g).to(device)
+    dout = torch.randn(bt, t_len, d, generator=g).to(device)
+
+    def timed(fn, k=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(k):
+            fn()
+        s1.record()
+        torch.cuda.synchronize()
+        return s0.elapsed_time(s1) / k
+
+    f_ms = timed(lambda: _native.gate_fwd(y, z, dskip))
+    b_ms = timed(lambda: _native.gate_bwd(dout, y, z, dskip))
+
+    def unfused():
+        leaves = [t.detach().requires_grad_(True) for t in (y, z, dskip)]
+        out = gate_ref(*leaves)
+        return torch.autograd.grad(out, leaves, grad_outputs=dout)
+
+    u_ms = timed(unfused)
+    elems = bt * t_len * d
+    fwd_b, bwd_b = 12 * elems + 4 * d, 20 * elems + 8 * d
+    gbs = (fwd_b + bwd_b) / ((f_ms + b_ms) * 1e-3) / 1e9
+    return {"workload": f"(y + D) * silu(z) fwd + bwd at B{bt} T{t_len} D{d}, z strided",
+            "fwd_ms": f_ms, "bwd_ms": b_ms, "unfused_torch_ms": u_ms,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": gbs / hbm_gbs, "algorithmic_bytes": fwd_b + bwd_b}}
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -668,7 +715,8 @@ def main():
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode-step timing")
-    ap.add_argument("--no-proj", action="store_true", help="skip the fused-prologue timing")
+    ap.add_argument("--no-proj", action="store_true",
+                    help="skip the fused prologue / gate epilogue timings")
     ap.add_argument("--shard", choices=("batch", "channel"), default=None,
                     help="multi-GPU split (default: channel for c4, batch otherwise)")
     ap.add_argument("--no-stride64", action="store_true",

@@ -53,7 +53,7 @@ extern "C" {
                                       (reported by mms_device_status)                    */
 
 /* Version of the ABI in this header (major * 100 + minor). */
-#define MMS_ABI_VERSION 102
+#define MMS_ABI_VERSION 103
 int mms_abi_version(void);
 
 /* Human-readable text for an MMS_* status. Never NULL. */
@@ -155,6 +155,26 @@ int mms_bwd_noalloc(const float *x, const float *dt, const float *aneg,
 int mms_step(const float *x, const float *dt, const float *aneg,
              const float *B, const float *C, float *h, float *y,
              int Bt, int D, int N, void *stream);
+
+/*
+ * Gate epilogue of the Mamba block, one kernel each way (reference
+ * mamba_metal/model.py:255-256 runs it as separate PyTorch ops):
+ *     out = (y + d_skip) * silu(z),   silu(z) = z * sigmoid(z)
+ * y, out, dout, dy, dz are (Bt, T, D) contiguous; z is (Bt, T, D) with row
+ * stride ldz >= D elements (the block's z is a half of in_proj's output);
+ * d_skip, d_dskip are (D,).
+ * mms_gate_bwd writes dy = dout * silu(z), dz = dout * (y + d_skip) * silu'(z)
+ * and d_dskip = sum over (Bt, T) of dy (fixed order, through a caller
+ * workspace of mms_gate_workspace_size() bytes, 16-byte aligned).
+ * No counterpart in the reference.
+ */
+size_t mms_gate_workspace_size(int Bt, int T, int D);
+int mms_gate_fwd(const float *y, const float *z, long long ldz, const float *d_skip,
+                 float *out, int Bt, int T, int D, void *stream);
+int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ldz,
+                 const float *d_skip, float *dy, float *dz, float *d_dskip,
+                 void *workspace, size_t workspace_bytes,
+                 int Bt, int T, int D, void *stream);
 
 /*
  * Device-side status of the kernels launched so far, for failure detection.

@@ -146,6 +146,43 @@ int mms_step(const float *x, const float *dt, const float *aneg, const float *B,
                                                                                   : MMS_ERR_CUDA;
 }
 
+size_t mms_gate_workspace_size(int Bt, int T, int D)
+{
+    if (Bt < 1 || T < 1 || D < 1) return 0;
+    return mms::gate_workspace_bytes((long long)Bt * T, D);
+}
+
+int mms_gate_fwd(const float *y, const float *z, long long ldz, const float *d_skip, float *out,
+                 int Bt, int T, int D, void *stream)
+{
+    if (Bt < 1 || T < 1 || D < 1 || ldz < D || !y || !z || !d_skip || !out)
+        return MMS_ERR_INVALID_ARG;
+    if (!aligned(y, 4) || !aligned(z, 4) || !aligned(d_skip, 4) || !aligned(out, 4))
+        return MMS_ERR_MISALIGNED;
+    return mms::launch_gate_fwd(y, z, ldz, d_skip, out, (long long)Bt * T, D,
+                                static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                  : MMS_ERR_CUDA;
+}
+
+int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ldz,
+                 const float *d_skip, float *dy, float *dz, float *d_dskip, void *workspace,
+                 size_t workspace_bytes, int Bt, int T, int D, void *stream)
+{
+    if (Bt < 1 || T < 1 || D < 1 || ldz < D || !dout || !y || !z || !d_skip || !dy || !dz ||
+        !d_dskip)
+        return MMS_ERR_INVALID_ARG;
+    if (!aligned(dout, 4) || !aligned(y, 4) || !aligned(z, 4) || !aligned(d_skip, 4) ||
+        !aligned(dy, 4) || !aligned(dz, 4) || !aligned(d_dskip, 4))
+        return MMS_ERR_MISALIGNED;
+    if (!workspace || workspace_bytes < mms::gate_workspace_bytes((long long)Bt * T, D))
+        return MMS_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return MMS_ERR_MISALIGNED;
+    return mms::launch_gate_bwd(dout, y, z, ldz, d_skip, dy, dz, d_dskip, workspace,
+                                (long long)Bt * T, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? MMS_OK
+               : MMS_ERR_CUDA;
+}
+
 int mms_device_status(void)
 {
     if (cudaDeviceSynchronize() != cudaSuccess) return MMS_ERR_CUDA;

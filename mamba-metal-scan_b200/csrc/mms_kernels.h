@@ -128,6 +128,14 @@ cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const
 // 1 if a TMA-stage wait timed out since the last call (and clears it), 0 if
 // not, -1 if the flag could not be read.
 int w8_take_timeout();
+
+// Gate epilogue out = (y + D_skip) * silu(z) (mms_gate.cu); rows = Bt * T.
+size_t gate_workspace_bytes(long long rows, int D);
+cudaError_t launch_gate_fwd(const float *y, const float *z, long long ldz, const float *dskip,
+                            float *out, long long rows, int D, cudaStream_t stream);
+cudaError_t launch_gate_bwd(const float *dout, const float *y, const float *z, long long ldz,
+                            const float *dskip, float *dy, float *dz, float *dd, void *workspace,
+                            long long rows, int D, cudaStream_t stream);
 int fwd_take_timeout();
 // forward: chain the segment end states through the checkpoint slots
 cudaError_t launch_seg_combine_fwd(float *ckpt, int Bt, int nchunk, int S, int cps, size_t DN,

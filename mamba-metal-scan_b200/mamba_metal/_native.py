@@ -36,6 +36,10 @@ SIGNATURES = {
     "mms_bwd_noalloc": ([_P] * 12 + [_I] * 5 + [_P], _I),
     "mms_step": ([_P] * 7 + [_I] * 3 + [_P], _I),
     "mms_device_status": ([], _I),
+    "mms_gate_workspace_size": ([_I] * 3, ctypes.c_size_t),
+    "mms_gate_fwd": ([_P, _P, ctypes.c_longlong] + [_P] * 2 + [_I] * 3 + [_P], _I),
+    "mms_gate_bwd": ([_P] * 3 + [ctypes.c_longlong] + [_P] * 5 + [ctypes.c_size_t] + [_I] * 3
+                     + [_P], _I),
     "mms_fwd_proj": ([_P] * 5 + [ctypes.c_float] * 2 + [_P] * 2 + [_I] * 5 + [_P], _I),
     "mms_bwd_proj": ([_P] * 7 + [ctypes.c_float] * 2 + [_P] * 6 + [ctypes.c_size_t] + [_I] * 5
                      + [_P], _I),
@@ -157,3 +161,28 @@ def step(x, dt, aneg, b_in, c_in, h):
 def device_status() -> int:
     """MMS_OK, or MMS_ERR_TIMEOUT if a kernel's bounded wait ran out since the last call."""
     return int(load().mms_device_status())
+
+
+def gate_fwd(y, z, d_skip):
+    """out = (y + d_skip) * silu(z) in one kernel; z may have a row stride."""
+    lib = load()
+    bt, t_len, d = y.shape
+    out = torch.empty_like(y)
+    rc = lib.mms_gate_fwd(_ptr(y), _ptr(z), z.stride(1), _ptr(d_skip), _ptr(out), bt, t_len, d,
+                          _stream(y.device))
+    _check(rc, "mms_gate_fwd")
+    return out
+
+
+def gate_bwd(dout, y, z, d_skip):
+    """(dy, dz, d_dskip) of gate_fwd in one kernel (plus a fixed-order reduction)."""
+    lib = load()
+    bt, t_len, d = y.shape
+    dy, dd = torch.empty_like(y), torch.empty_like(d_skip)
+    dz = torch.empty(y.shape, device=y.device, dtype=torch.float32)
+    nb = int(lib.mms_gate_workspace_size(bt, t_len, d))
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=y.device)
+    rc = lib.mms_gate_bwd(_ptr(dout), _ptr(y), _ptr(z), z.stride(1), _ptr(d_skip), _ptr(dy),
+                          _ptr(dz), _ptr(dd), _ptr(ws), nb, bt, t_len, d, _stream(y.device))
+    _check(rc, "mms_gate_bwd")
+    return dy, dz, dd

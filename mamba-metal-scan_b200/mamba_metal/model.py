@@ -30,8 +30,8 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from mamba_metal.scan import (selective_scan, selective_scan_proj, selective_scan_step,
-                              selective_scan_step_ref)
+from mamba_metal.scan import (gated_output, selective_scan, selective_scan_proj,
+                              selective_scan_step, selective_scan_step_ref)
 
 
 @dataclass
@@ -47,6 +47,7 @@ class MambaConfig:
     scan_chunk: int = 0       # time slice of the parallel_scan fallback; 0 = one pass
     scan_impl: str = "auto"   # 'auto' | 'cuda' | 'metal' | 'torch'
     fuse_proj: bool = True    # CUDA scan computes dt and softplus(A) itself (selective_scan_proj)
+    fuse_gate: bool = True    # (y + D_skip) * silu(z) as one CUDA kernel each way (gated_output)
     dt_min: float = 0.001
     dt_max: float = 0.1
     norm_eps: float = 1e-6
@@ -160,6 +161,7 @@ class MambaBlock(nn.Module):
         self.scan_chunk = cfg.scan_chunk
         self.scan_impl = cfg.scan_impl
         self.fuse_proj = cfg.fuse_proj
+        self.fuse_gate = cfg.fuse_gate
         self.dt_min, self.dt_max = cfg.dt_min, cfg.dt_max
         self.norm = RMSNorm(dm, cfg.norm_eps)
         self.in_proj = nn.Linear(dm, 2 * d_inner, bias=False)
@@ -246,6 +248,8 @@ class MambaBlock(nn.Module):
             y, h_last = self._scan(x, return_state=True)
             if cache is not None:
                 cache["h"], cache["h_owned"] = h_last, False
+        if self.fuse_gate and y.is_cuda and self.scan_impl != "torch":
+            return residual + self.out_proj(gated_output(y, z, self.D_skip, impl=self.scan_impl))
         y = y + self.D_skip
         return residual + self.out_proj(y * F.silu(z))
 

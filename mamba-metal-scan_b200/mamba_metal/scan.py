@@ -277,6 +277,61 @@ def selective_scan_proj(x: torch.Tensor, dt_logit: torch.Tensor, a_param: torch.
     return None
 
 
+# ------------------------------------------------------ gate epilogue (f3)
+
+def gate_ref(y, z, d_skip):
+    """(y + D_skip) * silu(z), the Mamba block's epilogue (reference model.py:255-256)."""
+    return (y + d_skip) * torch.nn.functional.silu(z)
+
+
+class GateCUDA(torch.autograd.Function):
+    """out = (y + d_skip) * silu(z) as one kernel each way (mms_gate_fwd / _bwd).
+
+    z may be a view with a row stride (the second half of in_proj's output);
+    backward returns dy, dz and d_skip's gradient (a fixed-order sum).
+    """
+
+    @staticmethod
+    def forward(ctx, y, z, d_skip):
+        if not (y.is_cuda and z.is_cuda and d_skip.is_cuda):
+            raise RuntimeError("the CUDA gate needs CUDA tensors")
+        if y.dtype != torch.float32 or z.dtype != torch.float32 or d_skip.dtype != torch.float32:
+            raise RuntimeError("the CUDA gate is fp32-only")
+        if y.dim() != 3 or z.shape != y.shape or d_skip.shape != (y.shape[2],):
+            raise ValueError(f"bad shapes: y {tuple(y.shape)}, z {tuple(z.shape)}, "
+                             f"D_skip {tuple(d_skip.shape)}")
+        y, d_skip = y.contiguous(), d_skip.contiguous()
+        bt, t_len, d = y.shape
+        # rows (b, t) must sit at one stride apart: contiguous channels, uniform rows
+        if not (z.stride(2) == 1 and z.stride(1) >= d and z.stride(0) == t_len * z.stride(1)):
+            z = z.contiguous()
+        ctx.save_for_backward(y, z, d_skip)
+        if y.numel() == 0:
+            return torch.empty_like(y)
+        with torch.cuda.device(y.device):
+            return _native.gate_fwd(y, z, d_skip)
+
+    @staticmethod
+    def backward(ctx, dout):
+        y, z, d_skip = ctx.saved_tensors
+        if y.numel() == 0:
+            return torch.zeros_like(y), torch.zeros_like(y), torch.zeros_like(d_skip)
+        with torch.cuda.device(y.device):
+            return _native.gate_bwd(dout.contiguous().float(), y, z, d_skip)
+
+
+def gated_output(y: torch.Tensor, z: torch.Tensor, d_skip: torch.Tensor, impl: str = "auto"):
+    """(y + d_skip) * silu(z): one CUDA kernel each way on CUDA tensors
+    ('auto', 'cuda', 'metal'), PyTorch ops otherwise or with 'torch'."""
+    if impl not in _IMPLS:
+        raise ValueError(f"unknown scan_impl {impl!r}; want 'auto', 'cuda', 'metal' or 'torch'")
+    if impl != "torch" and y.is_cuda:
+        return GateCUDA.apply(y, z, d_skip)
+    if impl in ("cuda", "metal"):
+        raise RuntimeError(f"scan_impl={impl!r} needs CUDA tensors; got device {y.device.type!r}")
+    return gate_ref(y, z, d_skip)
+
+
 # ------------------------------------------------------------ decode (one token)
 
 def selective_scan_step_ref(x, dt, aneg, b_in, c_in, h):
