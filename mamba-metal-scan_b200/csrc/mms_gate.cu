@@ -86,6 +86,7 @@ gate_bwd_kernel(const float *__restrict__ dout, const float *__restrict__ y,
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     float dv[4];
     for (int k = 0; k < 4; ++k) dv[k] = d + k < D ? dskip[d + k] : 0.f;
+#pragma unroll 4
     for (long long r = r0; r < r1; ++r) {
         const size_t o = (size_t)r * D + d, ozz = (size_t)r * ldz + d;
         float g[4], yy[4], zz[4];
