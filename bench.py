@@ -59,17 +59,31 @@ CONFIGS = {
 }
 
 
+def _splits(bt, t_len, d, n, k, dpb, ctas_per_sm):
+    """The library's time-segment rule (seg_plan / seg_plan_s16), restated."""
+    base = bt * (-(-d // dpb))
+    if base >= N_SM:
+        return False
+    nchunk = -(-t_len // k)
+    want = (ctas_per_sm * N_SM) // base
+    cps = max(-(-nchunk // want), 2, -(-64 // k))
+    return -(-nchunk // cps) >= 2
+
+
 def launches_per_step(bt, t_len, d, n, k):
-    """Kernels one mms_fwd + mms_bwd launch: 1 + 3, plus two segment passes in
-    each direction when the library splits time (its seg_plan rule, restated:
-    fewer than one 256/G-channel block per SM)."""
+    """Kernels of one mms_fwd + mms_bwd: 1 + 3, plus a local pass and a
+    combine in each direction that cuts time into segments."""
     g = 1
     while g < (n + 3) // 4:
         g *= 2
-    base = bt * (-(-d // (256 // g)))
-    nchunk = -(-t_len // k)
-    split = base < N_SM and nchunk > max(2, -(-64 // k))
-    return 4 + (4 if split else 0)
+    split_b = _splits(bt, t_len, d, n, k, 256 // g, 4)
+    if 8 < n <= 16 and bt * d >= N_SM * 128:
+        split_f = False                                   # whole-state forward, no split
+    elif 8 < n <= 16 and k >= 8 and d % 4 == 0 and _splits(bt, t_len, d, n, k, 128, 2):
+        split_f = True                                    # whole-state forward, segmented
+    else:
+        split_f = _splits(bt, t_len, d, n, k, 256 // g, 4)
+    return 4 + 2 * split_f + 2 * split_b
 
 
 def make_inputs(bt, t_len, d, n, seed, device):

@@ -209,12 +209,12 @@ __device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
 // on per-stage mbarriers, in an array-major layout [x TTxDPB][dt TTxDPB]
 // [B TTx16][C TTx16]; out-of-range steps, channels and states load as zeros,
 // like the cp.async path's zero fill.
-template <bool VEC, bool BULK, bool TMA, bool PROJ>
+template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG>
 __global__ void __launch_bounds__(S16_DPB, 2)
 fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, float *__restrict__ y,
-               float *__restrict__ ckpt, int T, int D, int N, int K,
+               float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps,
                const __grid_constant__ FwdMaps maps, Proj pj_in)
 {
     Proj pj = pj_in;                                       // the prologue only where used
@@ -238,6 +238,13 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     const bool dval = d < D;
     const int dcnt = min(DPB, D - d0);
     const int nchunk = (T + K - 1) / K;
+    // Time segment blockIdx.z of gridDim.z: steps [tb, te) = chunks
+    // [sg*cps, (sg+1)*cps); a single segment is the whole sequence.
+    // (SEG false: one segment, compiled without the segment bookkeeping)
+    const int sg = SEG ? (int)blockIdx.z : 0, nsg = SEG ? (int)gridDim.z : 1;
+    const int tb = SEG ? sg * L : 0, te = SEG ? min(T, tb + L) : T;
+    // the combine left the checkpoint at this segment's end; it is not rewritten
+    const int ck_keep = SEG && sg + 1 < nsg ? (sg + 1) * cps - 1 : -1;
 
     // -Aneg * log2(e) for the 16 states (zero past N): dA = 2^(dt * nan2).
     float2 nan2[8], h[8];
@@ -258,10 +265,20 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
     float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N;
     float *yb = y + (size_t)b * T * D + d;
+    if (SEG && sg > 0 && dval) {                           // state entering the segment
+        const float *src = ckb + (size_t)(sg * cps - 1) * D * N;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (4 * q < N) {
+                const float4 w = *reinterpret_cast<const float4 *>(src + 4 * q);
+                h[2 * q] = lo(w);
+                h[2 * q + 1] = hi(w);
+            }
+    }
 
     // BULK: send tile kp's y rows and its (up to two) checkpoint slabs.
     auto send = [&](int kp, int nck, int ck0, int ck1) {
-        const int t0p = kp * TT, rows = min(TT, T - t0p);
+        const int t0p = tb + kp * TT, rows = min(TT, te - t0p);
         const float *ysrc = ys + (kp & 1) * TT * DPB;
         for (int r = 0; r < rows; ++r)
             bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB, dcnt * 4u);
@@ -278,18 +295,20 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
             if (tid == 0) {
                 const uint32_t bar = bars + 8 * buf, dst = smem_u32(tile);
                 mbar_expect(bar, S16Shape::TILE_BYTES);
-                tma3(dst, &maps.x, d0, kt * TT, b, bar);
-                tma3(dst + 4 * DOFF, &maps.dt, d0, kt * TT, b, bar);
-                tma3(dst + 4 * BOFF, &maps.B, 0, kt * TT, b, bar);
-                tma3(dst + 4 * COFF, &maps.C, 0, kt * TT, b, bar);
+                tma3(dst, &maps.x, d0, tb + kt * TT, b, bar);
+                tma3(dst + 4 * DOFF, &maps.dt, d0, tb + kt * TT, b, bar);
+                tma3(dst + 4 * BOFF, &maps.B, 0, tb + kt * TT, b, bar);
+                tma3(dst + 4 * COFF, &maps.C, 0, tb + kt * TT, b, bar);
             }
         } else {
-            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tile, xb, dtb, dtb, Bb, Cb, kt * TT,
-                                                    min(TT, T - kt * TT), d0, D, N, tid);
+            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tile, xb, dtb, dtb, Bb, Cb, tb + kt * TT,
+                                                    min(TT, te - tb - kt * TT), d0, D, N, tid);
         }
     };
 
-    const int ntiles = (T + TT - 1) / TT;
+    // Rows past te (TMA: the next segment's steps; cp.async: zeros) move the
+    // state on, but nothing past te is stored.
+    const int ntiles = (te - tb + TT - 1) / TT;
     if constexpr (TMA) {
         if (tid == 0) {
             for (int s = 0; s < FWD_STAGES; ++s) mbar_init(bars + 8 * s, 1);
@@ -303,8 +322,8 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         cp_commit();
     }
 
-    int next_ck = min(K, T) - 1;
-    int chunk = 0;
+    int next_ck = min(tb + K, T) - 1;
+    int chunk = sg * cps;
     int nck = 0, ck0 = 0, ck1 = 0;                         // checkpoints of the current tile
     int pnck = 0, pck0 = 0, pck1 = 0;                      // ... of the previous tile
     for (int k = 0; k < ntiles; ++k) {
@@ -328,7 +347,7 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
 
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
         float *yrow = ys + (k & 1) * TT * DPB + tid;
-        const int t0 = k * TT;
+        const int t0 = tb + k * TT;
         nck = 0;
 #pragma unroll 4
         for (int j = 0; j < TT; ++j) {
@@ -356,15 +375,16 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
             for (int q = 1; q < MMS_FWD_ACC; ++q) acc[0] = add2(acc[0], acc[q]);
             const int t = t0 + j;
             if constexpr (BULK) yrow[j * DPB] = acc[0].x + acc[0].y;
-            else if (dval && t < T) yb[(size_t)t * D] = acc[0].x + acc[0].y;
-            if (t == next_ck) {                            // uniform across the CTA
+            else if (dval && t < te) yb[(size_t)t * D] = acc[0].x + acc[0].y;
+            if (t == next_ck && (!SEG || t < te)) {        // uniform across the CTA
                 float *o = ckb + (size_t)chunk * D * N;
-                if (BULK && nck < 2) {
+                const bool keep = SEG && chunk == ck_keep;
+                if (BULK && nck < 2 && !keep) {
                     o = cks + ((k & 1) * 2 + nck) * DPB * N + tid * N;
                     if (nck == 0) ck0 = chunk; else ck1 = chunk;
                     ++nck;
                 }
-                if (dval) {
+                if (dval && !keep) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         if (4 * q < N)
@@ -389,24 +409,65 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     }
 }
 
-template <bool VEC, bool BULK, bool TMA, bool PROJ>
-static cudaError_t launch_fwd_s16_p(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
+// Time segments for the whole-state forward: its CTAs hold 128 channels and
+// run 2 per SM, so segments are cut when batch rows x 128-channel blocks
+// leave SMs without a CTA, aiming at one full wave.
+static SegPlan seg_plan_s16(int Bt, int T, int D, int K)
+{
+    const long long base = (long long)Bt * ((D + S16_DPB - 1) / S16_DPB);
+    const int nchunk = (T + K - 1) / K;
+    SegPlan p{1, nchunk};
+    if (base >= N_SM) return p;
+    const long long want = (2LL * N_SM) / base;
+    long long cps = (nchunk + want - 1) / want;
+    if (cps < 2) cps = 2;                           // P_s is kept in chunk cps-2
+    if (cps * K < 64) cps = (64 + K - 1) / K;
+    const long long S = (nchunk + cps - 1) / cps;
+    if (S < 2) return p;
+    p.S = (int)S;
+    p.cps = (int)cps;
+    return p;
+}
+
+template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG>
+static cudaError_t launch_fwd_s16_q(const FwdArgs &a, const FwdMaps &maps, SegPlan sp,
+                                    cudaStream_t stream)
 {
     const size_t smem = TMA ? S16Shape::SMEM_TMA : BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA, PROJ>,
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt);
-    fwd_kernel_s16<VEC, BULK, TMA, PROJ><<<grid, S16_DPB, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, maps, a.proj);
+    dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt, sp.S);
+    fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG><<<grid, S16_DPB, smem, stream>>>(
+        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, sp.cps * a.K, sp.cps, maps,
+        a.proj);
     return cudaGetLastError();
+}
+
+template <bool VEC, bool BULK, bool TMA, bool PROJ>
+static cudaError_t launch_fwd_s16_p(const FwdArgs &a, const FwdMaps &maps, SegPlan sp,
+                                    cudaStream_t stream)
+{
+    if (sp.S > 1) return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, true>(a, maps, sp, stream);
+    return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, false>(a, maps, sp, stream);
 }
 
 template <bool VEC, bool BULK, bool TMA>
 static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
 {
-    return a.proj.on ? launch_fwd_s16_p<VEC, BULK, TMA, true>(a, maps, stream)
-                     : launch_fwd_s16_p<VEC, BULK, TMA, false>(a, maps, stream);
+    const SegPlan sp = seg_plan_s16(a.Bt, a.T, a.D, a.K);
+    if (sp.S > 1) {
+        // local end states and decay products of segments 0..S-2, then the chain
+        const int nchunk = (a.T + a.K - 1) / a.K;
+        SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, sp.cps * a.K,
+                        0, sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj};
+        cudaError_t e = launch_seg_local(la, false, stream);
+        if (e != cudaSuccess) return e;
+        e = launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N, stream);
+        if (e != cudaSuccess) return e;
+    }
+    return a.proj.on ? launch_fwd_s16_p<VEC, BULK, TMA, true>(a, maps, sp, stream)
+                     : launch_fwd_s16_p<VEC, BULK, TMA, false>(a, maps, sp, stream);
 }
 
 #ifndef MMS_FWD_BULK
@@ -489,7 +550,12 @@ static cudaError_t launch_fwd_g(const FwdArgs &a, cudaStream_t stream)
 
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)
 {
-    if (groups_for(a.N) == 4 && (long long)a.Bt * a.D >= S16_MIN_CHANNELS)
+    // whole-state kernel: enough channels, or few channels but long enough to
+    // cut into time segments (then it needs 16-byte rows for its TMA / bulk path)
+    if (groups_for(a.N) == 4 &&
+        ((long long)a.Bt * a.D >= S16_MIN_CHANNELS ||
+         (seg_plan_s16(a.Bt, a.T, a.D, a.K).S > 1 && a.K >= 8 && vec_ok(a.D, a.x, a.dt) &&
+          vec_ok(a.D, a.y, a.y))))
         return launch_fwd_s16(a, stream);
     switch (groups_for(a.N)) {
     case 1: return launch_fwd_g<1>(a, stream);
