@@ -452,7 +452,7 @@ __device__ __forceinline__ void store_dacc(const Lane<G> &L, const Adjoint &A, f
 }
 
 // General backward: any checkpoint stride K (see the file comment).
-template <int G, bool VEC>
+template <int G, bool VEC, bool PROJ>
 __global__ void __launch_bounds__(BWD_THREADS, MMS_BWD_MINB)
 bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
@@ -460,8 +460,10 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ ckpt, float *__restrict__ dx,
            float *__restrict__ ddt, float *__restrict__ part_bc,
            float *__restrict__ part_a, float *subck, const float *__restrict__ seg_e,
-           int T, int D, int N, int K, int nblk, int nsegk, int cps, Proj pj)
+           int T, int D, int N, int K, int nblk, int nsegk, int cps, Proj pj_in)
 {
+    Proj pj = pj_in;                 // the prologue is compiled in only where it is used
+    pj.on = PROJ;
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
     extern __shared__ __align__(16) float smem[];
@@ -596,7 +598,7 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 // Backward for checkpoint stride K == GRP: every chunk is one group whose
 // entry state is the forward's checkpoint, so there is no recompute pass and
 // no slot storage; groups are simply chunks nchunk-1 .. 0.
-template <int G, bool VEC>
+template <int G, bool VEC, bool PROJ>
 __global__ void __launch_bounds__(BWD_THREADS, MMS_BWD_K8_MINB)
 bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
@@ -604,8 +606,10 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
               const float *__restrict__ ckpt, float *__restrict__ dx,
               float *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
-              int T, int D, int N, int nblk, int cps, Proj pj)
+              int T, int D, int N, int nblk, int cps, Proj pj_in)
 {
+    Proj pj = pj_in;                 // the prologue is compiled in only where it is used
+    pj.on = PROJ;
     using S = BwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD;
     extern __shared__ __align__(16) float smem[];
@@ -756,8 +760,8 @@ BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K)
     return w;
 }
 
-template <int G, bool VEC>
-static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaStream_t stream)
+template <int G, bool VEC, bool PROJ>
+static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaStream_t stream)
 {
     using S = BwdShape<G>;
     cudaError_t e;
@@ -781,17 +785,17 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     if (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
-        e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM_K8);
         if (e != cudaSuccess) return e;
-        bwd_kernel_k8<G, VEC><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
+        bwd_kernel_k8<G, VEC, PROJ><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e,
             a.T, a.D, a.N, w.nblk, sp.cps, a.proj);
     } else {
-        e = cudaFuncSetAttribute(bwd_kernel<G, VEC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(bwd_kernel<G, VEC, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)S::SMEM);
         if (e != cudaSuccess) return e;
-        bwd_kernel<G, VEC><<<grid, BWD_THREADS, S::SMEM, stream>>>(
+        bwd_kernel<G, VEC, PROJ><<<grid, BWD_THREADS, S::SMEM, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck, seg_e,
             a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps, a.proj);
     }
@@ -804,6 +808,13 @@ static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaSt
     const int ra = (int)((dn + 255) / 256 < 148 * 16 ? (dn + 255) / 256 : 148 * 16);
     reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt * sp.S, dn, a.aneg, a.proj.on);
     return cudaGetLastError();
+}
+
+template <int G, bool VEC>
+static cudaError_t launch_bwd_gv(const BwdArgs &a, const BwdWorkspace &w, cudaStream_t stream)
+{
+    return a.proj.on ? launch_bwd_gvp<G, VEC, true>(a, w, stream)
+                     : launch_bwd_gvp<G, VEC, false>(a, w, stream);
 }
 
 template <int G>

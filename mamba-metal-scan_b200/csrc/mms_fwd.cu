@@ -38,13 +38,15 @@ struct FwdShape {
                                                     + (size_t)TT * DPB * G);
 };
 
-template <int G, bool VEC>
+template <int G, bool VEC, bool PROJ>
 __global__ void __launch_bounds__(FWD_THREADS, 2)
 fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
            const float *__restrict__ Cm, float *__restrict__ y,
-           float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps, Proj pj)
+           float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps, Proj pj_in)
 {
+    Proj pj = pj_in;                 // the prologue is compiled in only where it is used
+    pj.on = PROJ;
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
     extern __shared__ __align__(128) float smem[];
@@ -516,11 +518,11 @@ int fwd_take_timeout()
     return v ? 1 : 0;
 }
 
-template <int G, bool VEC>
-static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
+template <int G, bool VEC, bool PROJ>
+static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
 {
     using S = FwdShape<G>;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<G, VEC>,
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<G, VEC, PROJ>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     if (e != cudaSuccess) return e;
     const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K);
@@ -536,9 +538,15 @@ static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
             return e;
     }
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt, sp.S);
-    fwd_kernel<G, VEC><<<grid, FWD_THREADS, S::SMEM, stream>>>(
+    fwd_kernel<G, VEC, PROJ><<<grid, FWD_THREADS, S::SMEM, stream>>>(
         a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps, a.proj);
     return cudaGetLastError();
+}
+
+template <int G, bool VEC>
+static cudaError_t launch_fwd_gv(const FwdArgs &a, cudaStream_t stream)
+{
+    return a.proj.on ? launch_fwd_gvp<G, VEC, true>(a, stream) : launch_fwd_gvp<G, VEC, false>(a, stream);
 }
 
 template <int G>

@@ -45,14 +45,16 @@ struct SegLocalShape {
 // One CTA: DPB channels of batch row blockIdx.z, segment s_first + blockIdx.y.
 // Forward: v <- dA*v + dt*x*B over the segment, ascending.
 // Backward: g <- dA_next*g + dy*C, descending; v = dA_{t0} * g_{t0} at the end.
-template <int G, bool BWD, bool VEC>
+template <int G, bool BWD, bool VEC, bool PROJ>
 __global__ void __launch_bounds__(SEGL_THREADS, 2)
 seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
                  const float *__restrict__ aneg, const float *__restrict__ row,
                  float *__restrict__ vout, float *__restrict__ pout,
                  int T, int D, int N, int L, int s_first, int bplanes, int splanes,
-                 int voff, int poff, Proj pj)
+                 int voff, int poff, Proj pj_in)
 {
+    Proj pj = pj_in;                 // the prologue is compiled in only where it is used
+    pj.on = PROJ;
     using S = SegLocalShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, ROWF = S::ROWF, TT = SEGL_TT;
     extern __shared__ __align__(16) float smem[];
@@ -179,18 +181,25 @@ __global__ void seg_combine_bwd_kernel(float *__restrict__ E, const float *__res
     }
 }
 
-template <int G, bool BWD, bool VEC>
-static cudaError_t launch_local_gv(const SegLocalArgs &a, cudaStream_t stream)
+template <int G, bool BWD, bool VEC, bool PROJ>
+static cudaError_t launch_local_gvp(const SegLocalArgs &a, cudaStream_t stream)
 {
     using S = SegLocalShape<G>;
-    cudaError_t e = cudaFuncSetAttribute(seg_local_kernel<G, BWD, VEC>,
+    cudaError_t e = cudaFuncSetAttribute(seg_local_kernel<G, BWD, VEC, PROJ>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.nseg, a.Bt);
-    seg_local_kernel<G, BWD, VEC><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
+    seg_local_kernel<G, BWD, VEC, PROJ><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
         a.u, a.dt, a.aneg, a.row, a.vout, a.pout, a.T, a.D, a.N, a.L, a.s_first, a.bplanes,
         a.splanes, a.voff, a.poff, a.proj);
     return cudaGetLastError();
+}
+
+template <int G, bool BWD, bool VEC>
+static cudaError_t launch_local_gv(const SegLocalArgs &a, cudaStream_t stream)
+{
+    return a.proj.on ? launch_local_gvp<G, BWD, VEC, true>(a, stream)
+                     : launch_local_gvp<G, BWD, VEC, false>(a, stream);
 }
 
 template <int G>
