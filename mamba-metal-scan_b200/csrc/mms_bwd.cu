@@ -785,15 +785,13 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
     if (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
-        e = cudaFuncSetAttribute(bwd_kernel_k8<G, VEC, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)S::SMEM_K8);
+        e = smem_opt_in<bwd_kernel_k8<G, VEC, PROJ>>(S::SMEM_K8);
         if (e != cudaSuccess) return e;
         bwd_kernel_k8<G, VEC, PROJ><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e,
             a.T, a.D, a.N, w.nblk, sp.cps, a.proj);
     } else {
-        e = cudaFuncSetAttribute(bwd_kernel<G, VEC, PROJ>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)S::SMEM);
+        e = smem_opt_in<bwd_kernel<G, VEC, PROJ>>(S::SMEM);
         if (e != cudaSuccess) return e;
         bwd_kernel<G, VEC, PROJ><<<grid, BWD_THREADS, S::SMEM, stream>>>(
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck, seg_e,

@@ -478,8 +478,7 @@ cudaError_t launch_w8p(const BwdArgs &a, float *part_bc, float *part_a, const fl
                        int nblk, SegPlan sp, const W8Maps &maps, cudaStream_t stream)
 {
     const size_t smem = TMA ? W8Shape::SMEM_TMA : W8Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(bwd_kernel_w8<VEC, TMA, PROJ>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = smem_opt_in<bwd_kernel_w8<VEC, TMA, PROJ>>(smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
     bwd_kernel_w8<VEC, TMA, PROJ><<<grid, W8_THREADS, smem, stream>>>(

@@ -436,8 +436,7 @@ static cudaError_t launch_fwd_s16_q(const FwdArgs &a, const FwdMaps &maps, SegPl
                                     cudaStream_t stream)
 {
     const size_t smem = TMA ? S16Shape::SMEM_TMA : BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = smem_opt_in<fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG>>(smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt, sp.S);
     fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG><<<grid, S16_DPB, smem, stream>>>(
@@ -522,8 +521,7 @@ template <int G, bool VEC, bool PROJ>
 static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
 {
     using S = FwdShape<G>;
-    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<G, VEC, PROJ>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    cudaError_t e = smem_opt_in<fwd_kernel<G, VEC, PROJ>>(S::SMEM);
     if (e != cudaSuccess) return e;
     const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K);
     const int nchunk = (a.T + a.K - 1) / a.K;

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace mms {
 
 // The fused _proj prologue (reference mamba_metal/model.py:191-201): when
@@ -37,6 +39,23 @@ struct StepArgs {
     float *h, *y;
     int Bt, D, N;
 };
+
+// Opt a kernel into `bytes` of dynamic shared memory once per device: the
+// setting persists, and repeating it on every launch costs a driver call.
+// KERNEL is the kernel's address, so every kernel has its own flags.
+template <auto KERNEL>
+inline cudaError_t smem_opt_in(size_t bytes)
+{
+    static std::atomic<unsigned long long> done{0};         // one bit per device (< 64)
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(KERNEL, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_release);
+    return e;
+}
 
 // Lanes per channel: ceil(N/4) rounded up to a power of two (N in [4, 64]).
 inline int groups_for(int N)

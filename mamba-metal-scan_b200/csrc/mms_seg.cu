@@ -185,8 +185,7 @@ template <int G, bool BWD, bool VEC, bool PROJ>
 static cudaError_t launch_local_gvp(const SegLocalArgs &a, cudaStream_t stream)
 {
     using S = SegLocalShape<G>;
-    cudaError_t e = cudaFuncSetAttribute(seg_local_kernel<G, BWD, VEC, PROJ>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::SMEM);
+    cudaError_t e = smem_opt_in<seg_local_kernel<G, BWD, VEC, PROJ>>(S::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.nseg, a.Bt);
     seg_local_kernel<G, BWD, VEC, PROJ><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
