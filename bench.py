@@ -22,6 +22,7 @@ Printed (rank 0): one JSON line with the contract keys plus
   decode        the one-token step kernel at the config-4 decode shape
   proj          the scan with the dt / softplus(A) prologue fused into the kernels
   gate          the block's (y + D) * silu(z) epilogue, one kernel each way
+  bf16          the scan kernels with bf16 x, dt, y, dy, dx, ddt (fp32 arithmetic)
   clocks        nvidia-smi samples taken during the timed region
 `--impl reference` times only the reference CPU path (rank 0) and prints its line.
 """
@@ -400,6 +401,9 @@ def run_native(args, shape):
     if kk != 64 and not args.no_stride64:
         line["reference_stride"] = time_stride(lib, _native, (bt, t_len, d, n, 64), device,
                                                (x, dt, aneg, b_in, c_in, dy), stream)
+    if kk == 8 and n in (12, 16) and d % 8 == 0 and world == 1 and not args.no_bf16:
+        line["bf16"] = time_bf16(lib, _native, shape, device, (x, dt, aneg, b_in, c_in, dy),
+                                 stream, hbm_gbs)
     # e2e through the public API from pinned host buffers
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan, channel)
@@ -453,6 +457,54 @@ def time_stride(lib, _native, shape, device, ins, stream, k=20):
     f, b = ev[0].elapsed_time(ev[1]) / k, ev[1].elapsed_time(ev[2]) / k
     return {"chunk": kk, "fwd_ms": f, "bwd_ms": b, "value": bt * t_len * d / ((f + b) * 1e-3),
             "unit": UNIT, "note": "the reference's checkpoint stride, same inputs, kernels only"}
+
+
+def time_bf16(lib, _native, shape, device, ins, stream, hbm_gbs, k=20):
+    """Row f4: mms_fwd_bf16 / mms_bwd_bf16 kernel times on the same inputs with
+    x, dt, dy rounded to bf16 (y, dx, ddt stored as bf16; Aneg, B, C, ckpt,
+    dAneg, dB, dC fp32)."""
+    bt, t_len, d, n, kk = shape
+    x, dt, aneg, b_in, c_in, dy = (t.to(torch.bfloat16) if t.dim() == 3 and t.shape[-1] == d else t
+                                   for t in ins)
+    P = lambda t: t.data_ptr()  # noqa: E731
+    y = torch.empty_like(x)
+    ckpt = torch.empty(bt, (t_len + kk - 1) // kk, d, n, device=device)
+    grads = [torch.empty_like(x), torch.empty_like(x), torch.empty_like(aneg),
+             torch.empty_like(b_in), torch.empty_like(c_in)]
+    nb = _native.bwd_workspace_size(bt, t_len, d, n, kk)
+    ws = torch.empty(nb, dtype=torch.uint8, device=device)
+    sp = stream.cuda_stream
+
+    def fwd():
+        rc = lib.mms_fwd_bf16(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(y), P(ckpt),
+                              bt, t_len, d, n, kk, sp)
+        assert rc == 0, _native.status_string(rc)
+
+    def bwd():
+        rc = lib.mms_bwd_bf16(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(dy), P(ckpt),
+                              *(P(g) for g in grads), P(ws), nb, bt, t_len, d, n, kk, sp)
+        assert rc == 0, _native.status_string(rc)
+
+    for _ in range(3):
+        fwd()
+        bwd()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record(stream)
+    for _ in range(k):
+        fwd()
+    ev[1].record(stream)
+    for _ in range(k):
+        bwd()
+    ev[2].record(stream)
+    torch.cuda.synchronize()
+    f, b = ev[0].elapsed_time(ev[1]) / k, ev[1].elapsed_time(ev[2]) / k
+    btd, btn, dn = bt * t_len * d, bt * t_len * n, d * n
+    fwd_b = 2 * 3 * btd + 4 * (2 * btn + dn)
+    bwd_b = 2 * 5 * btd + 4 * (4 * btn + 2 * dn)
+    return {"fwd_ms": f, "bwd_ms": b, "value": btd / ((f + b) * 1e-3), "unit": UNIT,
+            "algorithmic_bytes": {"fwd": fwd_b, "bwd": bwd_b},
+            "bwd_hbm_frac": bwd_b / (b * 1e-3) / 1e9 / hbm_gbs,
+            "note": "bf16 x, dt, y, dy, dx, ddt; fp32 arithmetic, Aneg, B, C, ckpt; kernels only"}
 
 
 def run_e2e(args, shape, device, world, rank, selective_scan, channel=False):
@@ -733,6 +785,7 @@ def main():
                     help="skip the fused prologue / gate epilogue timings")
     ap.add_argument("--shard", choices=("batch", "channel"), default=None,
                     help="multi-GPU split (default: channel for c4, batch otherwise)")
+    ap.add_argument("--no-bf16", action="store_true", help="skip the bf16-storage side timing")
     ap.add_argument("--no-stride64", action="store_true",
                     help="skip the side timing at the reference's checkpoint stride")
     args = ap.parse_args()

@@ -36,6 +36,7 @@
 #define MMS_SCAN_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -51,9 +52,11 @@ extern "C" {
                                       MMS_NOALLOC_SCRATCH_BYTES                          */
 #define MMS_ERR_TIMEOUT 7          /* a kernel gave up waiting for its own staged copies
                                       (reported by mms_device_status)                    */
+#define MMS_ERR_UNSUPPORTED_BF16 8 /* the bf16 entry points need 8 < N <= 16, D % 8 == 0
+                                      and K == 8 (forward: K >= 8)                       */
 
 /* Version of the ABI in this header (major * 100 + minor). */
-#define MMS_ABI_VERSION 103
+#define MMS_ABI_VERSION 104
 int mms_abi_version(void);
 
 /* Human-readable text for an MMS_* status. Never NULL. */
@@ -175,6 +178,28 @@ int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ld
                  const float *d_skip, float *dy, float *dz, float *d_dskip,
                  void *workspace, size_t workspace_bytes,
                  int Bt, int T, int D, void *stream);
+
+/*
+ * The scan with bf16 storage for the (Bt, T, D) channel arrays: x, dt and y
+ * (forward), dy, dx and ddt (backward) hold bf16 bit patterns (uint16_t);
+ * Aneg, dAneg, B, C, dB, dC and ckpt stay float32, and every sum, product
+ * and exponential is computed in float32 as in mms_fwd / mms_bwd. Outputs
+ * are rounded to bf16 once, at the store. Halves the bytes of the six
+ * arrays that dominate the traffic.
+ * Shapes: 8 < N <= 16 (N = 12 or 16), D % 8 == 0, K == 8 for the backward
+ * and K >= 8 for the forward; otherwise MMS_ERR_UNSUPPORTED_BF16. The bf16
+ * arrays must be 16-byte aligned. Workspace as mms_bwd (same size function).
+ * No counterpart in the reference, which is float32-only
+ * (mamba_metal/scan.py:350-354).
+ */
+int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg,
+                 const float *B, const float *C, uint16_t *y, float *ckpt,
+                 int Bt, int T, int D, int N, int K, void *stream);
+int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg,
+                 const float *B, const float *C, const uint16_t *dy, const float *ckpt,
+                 uint16_t *dx, uint16_t *ddt, float *daneg, float *dB, float *dC,
+                 void *workspace, size_t workspace_bytes,
+                 int Bt, int T, int D, int N, int K, void *stream);
 
 /*
  * Device-side status of the kernels launched so far, for failure detection.

@@ -32,7 +32,7 @@ int fwd_impl(const float *x, const float *dt, const float *aneg, const float *B,
     if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
         !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
         return MMS_ERR_MISALIGNED;
-    mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, proj};
+    mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, proj, 0};
     return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
                                                                                  : MMS_ERR_CUDA;
 }
@@ -54,10 +54,22 @@ int bwd_impl(const float *x, const float *dt, const float *aneg, const float *B,
     if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
     if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
     mms::BwdArgs a{x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace,
-                   Bt, T, D, N, K, proj};
+                   Bt, T, D, N, K, proj, 0};
     return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
                                                                                  : MMS_ERR_CUDA;
 }
+
+// Shapes the bf16 entry points cover (the whole-state forward and the
+// 8-state backward, both staged by TMA in 16-byte rows).
+int check_bf16(int N, int D, int K, bool backward)
+{
+    if (N <= 8 || N > 16 || D % 8 != 0 || (backward ? K != 8 : K < 8)) return MMS_ERR_UNSUPPORTED_BF16;
+    return MMS_OK;
+}
+
+// pointers carried through the float-typed launcher structs
+const float *fp(const uint16_t *p) { return reinterpret_cast<const float *>(p); }
+float *fp(uint16_t *p) { return reinterpret_cast<float *>(p); }
 
 // dt = dt_min + (dt_max - dt_min) * sigmoid(logit) needs finite bounds in order.
 bool proj_ok(float dt_min, float dt_max)
@@ -82,6 +94,8 @@ const char *mms_status_string(int status)
     case MMS_ERR_MISALIGNED: return "misaligned pointer (B, C, Aneg, ckpt, dB, dC, dAneg need 16 bytes)";
     case MMS_ERR_CUDA: return "CUDA launch failed";
     case MMS_ERR_TIMEOUT: return "a kernel timed out waiting for its staged copies (results invalid)";
+    case MMS_ERR_UNSUPPORTED_BF16:
+        return "bf16 scan needs 8 < N <= 16, D % 8 == 0 and K == 8 (forward: K >= 8)";
     case MMS_ERR_TOO_LARGE:
         return "shape needs more workspace than mms_bwd_noalloc's static scratch "
                "(MMS_NOALLOC_SCRATCH_BYTES = 16 MiB); use mms_bwd with a caller workspace";
@@ -181,6 +195,45 @@ int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ld
                                 (long long)Bt * T, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
                ? MMS_OK
                : MMS_ERR_CUDA;
+}
+
+int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const float *B,
+                 const float *C, uint16_t *y, float *ckpt, int Bt, int T, int D, int N, int K,
+                 void *stream)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if ((rc = check_bf16(N, D, K, false))) return rc;
+    if (!x || !dt || !aneg || !B || !C || !y || !ckpt) return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(x, 16) || !aligned(dt, 16) || !aligned(y, 16))
+        return MMS_ERR_MISALIGNED;
+    mms::FwdArgs a{fp(x), fp(dt), aneg, B, C, fp(y), ckpt, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
+    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
+}
+
+int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const float *B,
+                 const float *C, const uint16_t *dy, const float *ckpt, uint16_t *dx, uint16_t *ddt,
+                 float *daneg, float *dB, float *dC, void *workspace, size_t workspace_bytes,
+                 int Bt, int T, int D, int N, int K, void *stream)
+{
+    int rc = check_shape(Bt, T, D, N, K);
+    if (rc) return rc;
+    if ((rc = check_bf16(N, D, K, true))) return rc;
+    if (!x || !dt || !aneg || !B || !C || !dy || !ckpt || !dx || !ddt || !daneg || !dB || !dC)
+        return MMS_ERR_INVALID_ARG;
+    if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
+        !aligned(daneg, 16) || !aligned(dB, 16) || !aligned(dC, 16) || !aligned(x, 16) ||
+        !aligned(dt, 16) || !aligned(dy, 16) || !aligned(dx, 16) || !aligned(ddt, 16))
+        return MMS_ERR_MISALIGNED;
+    const size_t need = mms::bwd_workspace_layout(Bt, T, D, N, K).total;
+    if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
+    mms::BwdArgs a{fp(x), fp(dt), aneg, B, C, fp(dy), ckpt, fp(dx), fp(ddt), daneg, dB, dC,
+                   workspace, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
+    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
+                                                                                 : MMS_ERR_CUDA;
 }
 
 int mms_device_status(void)

@@ -775,14 +775,14 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
     if (sp.S > 1) {
         // local adjoint carries of segments 1..S-1, then the chain (last to first)
         SegLocalArgs la{a.dy, a.dt, a.aneg, a.C, seg_e, seg_p, a.Bt, a.T, a.D, a.N,
-                        sp.cps * a.K, 1, sp.S - 1, sp.S, 1, 0, 0, a.proj};
+                        sp.cps * a.K, 1, sp.S - 1, sp.S, 1, 0, 0, a.proj, a.bf16};
         if ((e = launch_seg_local(la, true, stream)) != cudaSuccess) return e;
         if ((e = launch_seg_combine_bwd(seg_e, seg_p, a.Bt, sp.S, (size_t)a.D * a.N, stream)) !=
             cudaSuccess)
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
-    if (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K)) {
+    if (a.bf16 || (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K))) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
         e = smem_opt_in<bwd_kernel_k8<G, VEC, PROJ>>(S::SMEM_K8);
@@ -825,6 +825,11 @@ static cudaError_t launch_bwd_g(const BwdArgs &a, const BwdWorkspace &w, cudaStr
 cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream)
 {
     const BwdWorkspace w = bwd_workspace_layout(a.Bt, a.T, a.D, a.N, a.K);
+    if (a.bf16) {
+        // bf16 channel arrays: only the 8-state backward reads them (8 < N <= 16, K == 8)
+        if (!bwd_w8_applies(a.N, a.K)) return cudaErrorInvalidValue;
+        return launch_bwd_gvp<4, true, false>(a, w, stream);
+    }
     switch (groups_for(a.N)) {
     case 1: return launch_bwd_g<1>(a, w, stream);
     case 2: return launch_bwd_g<2>(a, w, stream);

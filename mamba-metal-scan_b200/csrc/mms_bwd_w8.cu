@@ -89,26 +89,41 @@ struct W8Shape {
 };
 static_assert(W8Shape::T_CK + W8_DPB * 16 == W8Shape::STAGEF, "stage layouts differ in size");
 
+// TMA stage for channel arrays of storage type E (float or bf16): x, dt, dy
+// take ARR floats each, then B, C [CH][16] and the entry slab [DPB][16] (fp32);
+// BYTES is what one stage's six loads bring.
+template <typename E>
+struct W8Tile {
+    static constexpr int ARR = W8_CH * W8_DPB * (int)sizeof(E) / 4;
+    static constexpr int BC = 3 * ARR;
+    static constexpr int CK = BC + 2 * W8_CH * 16;
+    static constexpr uint32_t BYTES = 4u * (CK + W8_DPB * 16);
+};
+static_assert(W8Tile<float>::BYTES == W8Shape::T_BYTES, "fp32 TMA stage is the full stage");
+
 __device__ __forceinline__ float2 shfl2x(float2 v, int m) {
     return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-// The rewrite: staged tile -> 4-step runs and permuted B/C. TMA selects the
-// stage layout: array-major (TMA) or one interleaved row per step (cp.async).
-template <bool TMA>
+// The rewrite: staged tile -> 4-step runs and permuted B/C (fp32 from here
+// on, whatever the storage type E of x, dt, dy). TMA selects the stage
+// layout: array-major (TMA) or one interleaved row per step (cp.async, fp32).
+template <bool TMA, typename E>
 __device__ __forceinline__ void w8_rewrite(const float *nat, float *der, int tid, const Proj &pj)
 {
+    static_assert(TMA || sizeof(E) == 4, "bf16 stages come by TMA");
     constexpr int DPB = W8_DPB, NROWF = W8Shape::NROWF, QF = W8Shape::QF, PF = W8Shape::PF;
-    constexpr int AROW = TMA ? DPB : NROWF;                      // step stride, channel arrays
-    constexpr int AOFF = TMA ? W8Shape::T_ARR : DPB;             // array stride
+    constexpr int AROW = TMA ? DPB : NROWF;                      // step stride, channel arrays (E)
+    constexpr int AOFF = TMA ? W8_CH * DPB : DPB;                // array stride (E)
     constexpr int BROW = TMA ? 16 : NROWF;                       // step stride, B and C
-    constexpr int BOFF = TMA ? W8Shape::T_BC : 3 * DPB;
+    constexpr int BOFF = TMA ? W8Tile<E>::BC : 3 * DPB;          // floats
     constexpr int BARR = TMA ? W8_CH * 16 : 16;                  // B -> C
     // x, dt, dy: der[a][q][c][k] = arr_a[4q + k][c]
     for (int e = tid; e < 3 * 2 * DPB; e += W8_THREADS) {
         const int a = e / (2 * DPB), q = (e / DPB) & 1, cc = e % DPB;
-        const float *src = nat + (4 * q) * AROW + a * AOFF + cc;
-        float4 v4 = make_float4(src[0], src[AROW], src[2 * AROW], src[3 * AROW]);
+        const E *src = reinterpret_cast<const E *>(nat) + (4 * q) * AROW + a * AOFF + cc;
+        float4 v4 = make_float4(to_f(src[0]), to_f(src[AROW]), to_f(src[2 * AROW]),
+                                to_f(src[3 * AROW]));
         if (pj.on && a == 1)        // prologue: dt from its logit
             v4 = make_float4(fmaf(pj.range, sigmoid_fast(v4.x), pj.lo), fmaf(pj.range, sigmoid_fast(v4.y), pj.lo),
                              fmaf(pj.range, sigmoid_fast(v4.z), pj.lo), fmaf(pj.range, sigmoid_fast(v4.w), pj.lo));
@@ -213,10 +228,10 @@ struct W8Adj {
     float2 gad[4], anx[4], dac[4];
 };
 
-// Rebuild quad q from hb, then walk it backwards.
-template <bool FULL>
+// Rebuild quad q from hb, then walk it backwards; dx / ddt go to outq (E).
+template <bool FULL, typename E>
 __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], const W8Lane &L,
-                                        W8Adj &A, int q, int nv, float *outq, int D, float *sd,
+                                        W8Adj &A, int q, int nv, E *outq, int D, float *sd,
                                         const Proj &pj)
 {
     float2 hv[4][4];
@@ -269,7 +284,7 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
             keep += __shfl_xor_sync(0xffffffffu, L.h ? v0 : v1, 1);
             // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
             if (pj.on && L.h) keep *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
-            if (L.dval) outq[(size_t)k * D] = keep;
+            if (L.dval) outq[(size_t)k * D] = from_f<E>(keep);
         }
         // dB|dC over the warp's 16 channels
         vb[0] = add2(vb[0], shfl2x(vb[2], 16));
@@ -295,14 +310,14 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
 // stages are filled by TMA tile loads from the tensor maps in `maps` (one
 // thread issues 6 loads per chunk; out-of-range steps, channels, states and
 // the chunk-0 entry state arrive as zeros) and complete on per-stage
-// mbarriers.
-template <bool VEC, bool TMA, bool PROJ>
+// mbarriers. E: storage type of x, dt, dy, dx, ddt (float, or bf16 with TMA).
+template <bool VEC, bool TMA, bool PROJ, typename E>
 __global__ void __launch_bounds__(W8_THREADS, MMS_BWD_W8_MINB)
-bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
+bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
-              const float *__restrict__ Cm, const float *__restrict__ dy,
-              const float *__restrict__ ckpt, float *__restrict__ dx,
-              float *__restrict__ ddt, float *__restrict__ part_bc,
+              const float *__restrict__ Cm, const E *__restrict__ dy,
+              const float *__restrict__ ckpt, E *__restrict__ dx,
+              E *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
               int T, int D, int N, int nblk, int cps, const __grid_constant__ W8Maps maps,
               Proj pj_in)
@@ -322,7 +337,7 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
     const int nchunk = (T + W8_CH - 1) / W8_CH;
     const size_t plane = (size_t)D * N;
     const size_t rowD = (size_t)L.b * T * D;
-    const float *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
+    const E *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
     const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
     const float *ckb = ckpt + (size_t)L.b * nchunk * plane;
     float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
@@ -333,14 +348,15 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
         if constexpr (TMA) {
             if (tid == 0) {
                 const uint32_t bar = bars + 8 * buf, dst = smem_u32(st);
-                mbar_expect(bar, W8Shape::T_BYTES);
+                using Q = W8Tile<E>;
+                mbar_expect(bar, Q::BYTES);
                 const int t0 = c * W8_CH;
                 tma3(dst, &maps.x, L.d0, t0, L.b, bar);
-                tma3(dst + 4 * W8Shape::T_ARR, &maps.dt, L.d0, t0, L.b, bar);
-                tma3(dst + 8 * W8Shape::T_ARR, &maps.dy, L.d0, t0, L.b, bar);
-                tma3(dst + 4 * W8Shape::T_BC, &maps.B, 0, t0, L.b, bar);
-                tma3(dst + 4 * (W8Shape::T_BC + W8_CH * 16), &maps.C, 0, t0, L.b, bar);
-                tma4(dst + 4 * W8Shape::T_CK, &maps.ck, 0, L.d0, c - 1, L.b, bar);
+                tma3(dst + 4 * Q::ARR, &maps.dt, L.d0, t0, L.b, bar);
+                tma3(dst + 8 * Q::ARR, &maps.dy, L.d0, t0, L.b, bar);
+                tma3(dst + 4 * Q::BC, &maps.B, 0, t0, L.b, bar);
+                tma3(dst + 4 * (Q::BC + W8_CH * 16), &maps.C, 0, t0, L.b, bar);
+                tma4(dst + 4 * Q::CK, &maps.ck, 0, L.d0, c - 1, L.b, bar);
             }
             return;
         }
@@ -397,9 +413,9 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
             }
         }
         const float *st = nat + (it % W8_NAT) * W8Shape::STAGEF;
-        w8_rewrite<TMA>(st, der, tid, pj);
+        w8_rewrite<TMA, E>(st, der, tid, pj);
         float2 hA[4];
-        L.load8(hA, st + (TMA ? W8Shape::T_CK : W8Shape::NATF) + L.c * 16, 16);
+        L.load8(hA, st + (TMA ? W8Tile<E>::CK : W8Shape::NATF) + L.c * 16, 16);
         if (c - 2 >= clo) {
             // the stage's previous chunk was read before the barrier above
             if (TMA && tid == 0) fence_async_smem();
@@ -411,16 +427,16 @@ bwd_kernel_w8(const float *__restrict__ x, const float *__restrict__ dt,
         const W8View v(der, L);
         const int t0 = c * W8_CH;
         const int nv = min(W8_CH, T - t0);
-        float *outb = (L.h ? ddt : dx) + rowD + (size_t)t0 * D + L.d;
+        E *outb = (L.h ? ddt : dx) + rowD + (size_t)t0 * D + L.d;
         // later group (steps 4..7) from the state after step 3, then the first group
         if (nv > 4) {
             float2 h4[4] = {hA[0], hA[1], hA[2], hA[3]};
             w8_advance(h4, L, v, 0);
-            if (nv == W8_CH) w8_walk<true>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
-            else w8_walk<false>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
-            w8_walk<true>(v, hA, L, A, 0, nv, outb, D, sd, pj);
+            if (nv == W8_CH) w8_walk<true, E>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
+            else w8_walk<false, E>(v, h4, L, A, 1, nv, outb + (size_t)4 * D, D, sd, pj);
+            w8_walk<true, E>(v, hA, L, A, 0, nv, outb, D, sd, pj);
         } else {
-            w8_walk<false>(v, hA, L, A, 0, nv, outb, D, sd, pj);
+            w8_walk<false, E>(v, hA, L, A, 0, nv, outb, D, sd, pj);
         }
     }
     cp_wait<0>();
@@ -468,22 +484,25 @@ bool build_maps(const BwdArgs &a, W8Maps *m)
     const int nchunk = (a.T + W8_CH - 1) / W8_CH;
     const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
     const cuuint32_t bK[4] = {16, W8_DPB, 1, 1};
-    return tma_encode(fn, &m->x, a.x, 3, dX, bX) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX) &&
-           tma_encode(fn, &m->dy, a.dy, 3, dX, bX) && tma_encode(fn, &m->B, a.B, 3, dB, bB) &&
+    const int ex = a.bf16 ? 2 : 4;
+    return tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
+           tma_encode(fn, &m->dy, a.dy, 3, dX, bX, ex) && tma_encode(fn, &m->B, a.B, 3, dB, bB) &&
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
-template <bool VEC, bool TMA, bool PROJ>
+template <bool VEC, bool TMA, bool PROJ, typename E = float>
 cudaError_t launch_w8p(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                        int nblk, SegPlan sp, const W8Maps &maps, cudaStream_t stream)
 {
     const size_t smem = TMA ? W8Shape::SMEM_TMA : W8Shape::SMEM;
-    cudaError_t e = smem_opt_in<bwd_kernel_w8<VEC, TMA, PROJ>>(smem);
+    cudaError_t e = smem_opt_in<bwd_kernel_w8<VEC, TMA, PROJ, E>>(smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + W8_DPB - 1) / W8_DPB, a.Bt, sp.S);
-    bwd_kernel_w8<VEC, TMA, PROJ><<<grid, W8_THREADS, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e, a.T, a.D,
-        a.N, nblk, sp.cps, maps, a.proj);
+    auto cE = [](const float *p) { return reinterpret_cast<const E *>(p); };
+    auto mE = [](float *p) { return reinterpret_cast<E *>(p); };
+    bwd_kernel_w8<VEC, TMA, PROJ, E><<<grid, W8_THREADS, smem, stream>>>(
+        cE(a.x), cE(a.dt), a.aneg, a.B, a.C, cE(a.dy), a.ckpt, mE(a.dx), mE(a.ddt), part_bc, part_a,
+        seg_e, a.T, a.D, a.N, nblk, sp.cps, maps, a.proj);
     return cudaGetLastError();
 }
 
@@ -502,6 +521,14 @@ cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const
 {
     W8Maps maps;
     memset(&maps, 0, sizeof(maps));
+    if (a.bf16) {
+        // bf16 channel arrays: TMA staging only (D % 8 == 0, aligned arrays)
+        if (a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt, a.dy) ||
+            !vec_ok(a.D, a.dx, a.ddt) || !build_maps(a, &maps))
+            return cudaErrorInvalidValue;
+        return launch_w8p<true, true, false, __nv_bfloat16>(a, part_bc, part_a, seg_e, nblk, sp,
+                                                             maps, stream);
+    }
     if (!vec_ok(a.D, a.x, a.dt, a.dy))
         return launch_w8<false, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
     if (MMS_BWD_TMA && build_maps(a, &maps))

@@ -1,6 +1,7 @@
 // Shared device helpers for the sm_100a selective-scan kernels.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -33,6 +34,16 @@ __device__ __forceinline__ float sigmoid_fast(float z) {
 // softplus(a) = log(1 + e^a), = a once e^a dwarfs 1 in fp32.
 __device__ __forceinline__ float softplus(float a) {
     return a > 20.f ? a : log1pf(expf(a));
+}
+
+// Storage element of the (B, T, D) channel arrays: float, or bf16 for the
+// bf16 entry points (the arithmetic is fp32 either way).
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename E>
+__device__ __forceinline__ E from_f(float v) {
+    if constexpr (sizeof(E) == 4) return v;
+    else return __float2bfloat16_rn(v);
 }
 
 __device__ __forceinline__ float4 ld4(const float *p) {

@@ -192,6 +192,15 @@ struct S16Shape {
     static constexpr uint32_t TILE_BYTES = sizeof(float) * S16_TT * ROWF;
 };
 
+// TMA tile of channel-array storage type E: x and dt take XF floats each,
+// then B and C (fp32) [TT][16] each; BYTES is what one tile's four loads bring.
+template <typename E>
+struct S16Tile {
+    static constexpr int XF = S16_TT * S16_DPB * (int)sizeof(E) / 4;
+    static constexpr uint32_t BYTES = 4u * (2 * XF + 2 * S16_TT * 16);
+};
+static_assert(S16Tile<float>::BYTES == S16Shape::TILE_BYTES, "fp32 TMA tile is the full tile");
+
 // Tensor maps of the TMA staging path: x, dt (D, T, Bt) with 128 x 16 boxes,
 // B, C (N, T, Bt) with 16 x 16 boxes.
 struct FwdMaps {
@@ -211,25 +220,30 @@ __device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
 // on per-stage mbarriers, in an array-major layout [x TTxDPB][dt TTxDPB]
 // [B TTx16][C TTx16]; out-of-range steps, channels and states load as zeros,
 // like the cp.async path's zero fill.
-template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG>
+// E: storage type of x, dt and y (float, or bf16 with TMA staging only).
+template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG, typename E>
 __global__ void __launch_bounds__(S16_DPB, 2)
-fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
+fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
-               const float *__restrict__ Cm, float *__restrict__ y,
+               const float *__restrict__ Cm, E *__restrict__ y,
                float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps,
                const __grid_constant__ FwdMaps maps, Proj pj_in)
 {
     Proj pj = pj_in;                                       // the prologue only where used
     pj.on = PROJ;
+    static_assert(sizeof(E) == 4 || (TMA && BULK), "bf16 arrays take the TMA / bulk path");
     constexpr int DPB = S16Shape::DPB, ROWF = S16Shape::ROWF, TT = S16_TT;
-    // where step j of a tile keeps x, dt, B, C (floats from the tile start)
+    constexpr int XF = S16Tile<E>::XF;
+    // where step j of a tile keeps x, dt (elements of E from their region's
+    // start), B, C (floats); region offsets in floats from the tile start
     constexpr int XROW = TMA ? DPB : ROWF, XOFF = 0;
-    constexpr int DOFF = TMA ? TT * DPB : DPB;
-    constexpr int BROW = TMA ? 16 : ROWF, BOFF = TMA ? 2 * TT * DPB : 2 * DPB;
-    constexpr int COFF = TMA ? 2 * TT * DPB + TT * 16 : 2 * DPB + 16;
+    constexpr int DOFF = TMA ? XF : DPB;
+    constexpr int BROW = TMA ? 16 : ROWF, BOFF = TMA ? 2 * XF : 2 * DPB;
+    constexpr int COFF = TMA ? 2 * XF + TT * 16 : 2 * DPB + 16;
     extern __shared__ __align__(128) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
-    float *ys = smem + S16Shape::TILEF;                    // BULK: [2][TT][DPB]
+    float *ys = smem + S16Shape::TILEF;                    // BULK: [2][TT][DPB] of E
+    E *yse = reinterpret_cast<E *>(ys);
     float *cks = ys + S16Shape::YF;                        // BULK: [2][2][DPB*N]
     const uint32_t bars = smem_u32(cks + S16Shape::CKF);   // TMA: FWD_STAGES barriers
 
@@ -263,10 +277,10 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         h[p] = f2(0.f, 0.f);
     }
 
-    const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
+    const E *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
     float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N;
-    float *yb = y + (size_t)b * T * D + d;
+    E *yb = y + (size_t)b * T * D + d;
     if (SEG && sg > 0 && dval) {                           // state entering the segment
         const float *src = ckb + (size_t)(sg * cps - 1) * D * N;
 #pragma unroll
@@ -281,9 +295,10 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
     // BULK: send tile kp's y rows and its (up to two) checkpoint slabs.
     auto send = [&](int kp, int nck, int ck0, int ck1) {
         const int t0p = tb + kp * TT, rows = min(TT, te - t0p);
-        const float *ysrc = ys + (kp & 1) * TT * DPB;
+        const E *ysrc = yse + (kp & 1) * TT * DPB;
         for (int r = 0; r < rows; ++r)
-            bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB, dcnt * 4u);
+            bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB,
+                       dcnt * (uint32_t)sizeof(E));
         for (int i = 0; i < nck; ++i)
             bulk_store(ckpt + ((size_t)b * nchunk + (i ? ck1 : ck0)) * D * N + (size_t)d0 * N,
                        cks + ((kp & 1) * 2 + i) * DPB * N, (uint32_t)dcnt * N * 4u);
@@ -296,7 +311,7 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         if constexpr (TMA) {
             if (tid == 0) {
                 const uint32_t bar = bars + 8 * buf, dst = smem_u32(tile);
-                mbar_expect(bar, S16Shape::TILE_BYTES);
+                mbar_expect(bar, S16Tile<E>::BYTES);
                 tma3(dst, &maps.x, d0, tb + kt * TT, b, bar);
                 tma3(dst + 4 * DOFF, &maps.dt, d0, tb + kt * TT, b, bar);
                 tma3(dst + 4 * BOFF, &maps.B, 0, tb + kt * TT, b, bar);
@@ -348,14 +363,16 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
         cp_commit();
 
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
-        float *yrow = ys + (k & 1) * TT * DPB + tid;
+        const E *tx = reinterpret_cast<const E *>(tile + XOFF);
+        const E *tdt = reinterpret_cast<const E *>(tile + DOFF);
+        E *yrow = yse + (k & 1) * TT * DPB + tid;
         const int t0 = tb + k * TT;
         nck = 0;
 #pragma unroll 4
         for (int j = 0; j < TT; ++j) {
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = tile[XOFF + j * XROW + tid];
-            float dtv = tile[DOFF + j * XROW + tid];
+            const float xv = to_f(tx[j * XROW + tid]);
+            float dtv = to_f(tdt[j * XROW + tid]);
             if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
             const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW);
             const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
@@ -376,8 +393,8 @@ fwd_kernel_s16(const float *__restrict__ x, const float *__restrict__ dt,
 #pragma unroll
             for (int q = 1; q < MMS_FWD_ACC; ++q) acc[0] = add2(acc[0], acc[q]);
             const int t = t0 + j;
-            if constexpr (BULK) yrow[j * DPB] = acc[0].x + acc[0].y;
-            else if (dval && t < te) yb[(size_t)t * D] = acc[0].x + acc[0].y;
+            if constexpr (BULK) yrow[j * DPB] = from_f<E>(acc[0].x + acc[0].y);
+            else if (dval && t < te) yb[(size_t)t * D] = from_f<E>(acc[0].x + acc[0].y);
             if (t == next_ck && (!SEG || t < te)) {        // uniform across the CTA
                 float *o = ckb + (size_t)chunk * D * N;
                 const bool keep = SEG && chunk == ck_keep;
@@ -431,42 +448,47 @@ static SegPlan seg_plan_s16(int Bt, int T, int D, int K)
     return p;
 }
 
-template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG>
+template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG, typename E>
 static cudaError_t launch_fwd_s16_q(const FwdArgs &a, const FwdMaps &maps, SegPlan sp,
                                     cudaStream_t stream)
 {
     const size_t smem = TMA ? S16Shape::SMEM_TMA : BULK ? S16Shape::SMEM_BULK : S16Shape::SMEM;
-    cudaError_t e = smem_opt_in<fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG>>(smem);
+    cudaError_t e = smem_opt_in<fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E>>(smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt, sp.S);
-    fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG><<<grid, S16_DPB, smem, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, sp.cps * a.K, sp.cps, maps,
+    fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E><<<grid, S16_DPB, smem, stream>>>(
+        reinterpret_cast<const E *>(a.x), reinterpret_cast<const E *>(a.dt), a.aneg, a.B, a.C,
+        reinterpret_cast<E *>(a.y), a.ckpt, a.T, a.D, a.N, a.K, sp.cps * a.K, sp.cps, maps,
         a.proj);
     return cudaGetLastError();
 }
 
-template <bool VEC, bool BULK, bool TMA, bool PROJ>
+template <bool VEC, bool BULK, bool TMA, bool PROJ, typename E = float>
 static cudaError_t launch_fwd_s16_p(const FwdArgs &a, const FwdMaps &maps, SegPlan sp,
                                     cudaStream_t stream)
 {
-    if (sp.S > 1) return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, true>(a, maps, sp, stream);
-    return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, false>(a, maps, sp, stream);
+    if (sp.S > 1) return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, true, E>(a, maps, sp, stream);
+    return launch_fwd_s16_q<VEC, BULK, TMA, PROJ, false, E>(a, maps, sp, stream);
+}
+
+// local end states and decay products of segments 0..S-2, then the chain
+static cudaError_t fwd_s16_segments(const FwdArgs &a, SegPlan sp, cudaStream_t stream)
+{
+    if (sp.S <= 1) return cudaSuccess;
+    const int nchunk = (a.T + a.K - 1) / a.K;
+    SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, sp.cps * a.K,
+                    0, sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj, a.bf16};
+    cudaError_t e = launch_seg_local(la, false, stream);
+    if (e != cudaSuccess) return e;
+    return launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N, stream);
 }
 
 template <bool VEC, bool BULK, bool TMA>
 static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cudaStream_t stream)
 {
     const SegPlan sp = seg_plan_s16(a.Bt, a.T, a.D, a.K);
-    if (sp.S > 1) {
-        // local end states and decay products of segments 0..S-2, then the chain
-        const int nchunk = (a.T + a.K - 1) / a.K;
-        SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, sp.cps * a.K,
-                        0, sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj};
-        cudaError_t e = launch_seg_local(la, false, stream);
-        if (e != cudaSuccess) return e;
-        e = launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N, stream);
-        if (e != cudaSuccess) return e;
-    }
+    const cudaError_t e = fwd_s16_segments(a, sp, stream);
+    if (e != cudaSuccess) return e;
     return a.proj.on ? launch_fwd_s16_p<VEC, BULK, TMA, true>(a, maps, sp, stream)
                      : launch_fwd_s16_p<VEC, BULK, TMA, false>(a, maps, sp, stream);
 }
@@ -486,7 +508,8 @@ static bool fwd_maps(const FwdArgs &a, FwdMaps *m)
     const cuuint32_t bX[3] = {S16_DPB, S16_TT, 1};
     const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
     const cuuint32_t bB[3] = {16, S16_TT, 1};
-    return tma_encode(fn, &m->x, a.x, 3, dX, bX) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX) &&
+    const int ex = a.bf16 ? 2 : 4;
+    return tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
            tma_encode(fn, &m->B, a.B, 3, dB, bB) && tma_encode(fn, &m->C, a.C, 3, dB, bB);
 }
 
@@ -529,7 +552,7 @@ static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
     if (sp.S > 1) {
         // local end states and decay products of segments 0..S-2, then the chain
         SegLocalArgs la{a.x, a.dt, a.aneg, a.B, a.ckpt, a.ckpt, a.Bt, a.T, a.D, a.N, L, 0,
-                        sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj};
+                        sp.S - 1, nchunk, sp.cps, sp.cps - 1, sp.cps - 2, a.proj, a.bf16};
         if ((e = launch_seg_local(la, false, stream)) != cudaSuccess) return e;
         if ((e = launch_seg_combine_fwd(a.ckpt, a.Bt, nchunk, sp.S, sp.cps, (size_t)a.D * a.N,
                                         stream)) != cudaSuccess)
@@ -554,8 +577,25 @@ static cudaError_t launch_fwd_g(const FwdArgs &a, cudaStream_t stream)
                                   : launch_fwd_gv<G, false>(a, stream);
 }
 
+// bf16 channel arrays: always the whole-state kernel with TMA staging and
+// bulk y stores (the C ABI admits only shapes it covers: 8 < N <= 16,
+// K >= 8, D % 8 == 0, 16-byte aligned x, dt, y).
+static cudaError_t launch_fwd_bf16(const FwdArgs &a, cudaStream_t stream)
+{
+    FwdMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    if (groups_for(a.N) != 4 || a.K < 8 || a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt) ||
+        !vec_ok(a.D, a.y, a.y) || !fwd_maps(a, &maps))
+        return cudaErrorInvalidValue;
+    const SegPlan sp = seg_plan_s16(a.Bt, a.T, a.D, a.K);
+    const cudaError_t e = fwd_s16_segments(a, sp, stream);
+    if (e != cudaSuccess) return e;
+    return launch_fwd_s16_p<true, true, true, false, __nv_bfloat16>(a, maps, sp, stream);
+}
+
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)
 {
+    if (a.bf16) return launch_fwd_bf16(a, stream);
     // whole-state kernel: enough channels, or few channels but long enough to
     // cut into time segments (then it needs 16-byte rows for its TMA / bulk path)
     if (groups_for(a.N) == 4 &&

@@ -19,11 +19,15 @@ struct Proj {
     float lo, range;
 };
 
+// bf16 != 0: the (B, T, D) channel arrays (x, dt, y; dy, dx, ddt) hold bf16
+// values (the pointers are passed through as float * and reinterpreted by
+// the launchers); everything else stays fp32.
 struct FwdArgs {
     const float *x, *dt, *aneg, *B, *C;
     float *y, *ckpt;
     int Bt, T, D, N, K;
     Proj proj;
+    int bf16;
 };
 
 struct BwdArgs {
@@ -32,6 +36,7 @@ struct BwdArgs {
     void *workspace;
     int Bt, T, D, N, K;
     Proj proj;
+    int bf16;
 };
 
 struct StepArgs {
@@ -136,6 +141,7 @@ struct SegLocalArgs {
     float *vout, *pout;
     int Bt, T, D, N, L, s_first, nseg, bplanes, splanes, voff, poff;
     Proj proj;
+    int bf16;          // u and dt hold bf16
 };
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream);
 

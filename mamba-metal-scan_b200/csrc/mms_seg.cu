@@ -45,9 +45,10 @@ struct SegLocalShape {
 // One CTA: DPB channels of batch row blockIdx.z, segment s_first + blockIdx.y.
 // Forward: v <- dA*v + dt*x*B over the segment, ascending.
 // Backward: g <- dA_next*g + dy*C, descending; v = dA_{t0} * g_{t0} at the end.
-template <int G, bool BWD, bool VEC, bool PROJ>
+// E: storage type of u and dt (float or bf16; row is always fp32).
+template <int G, bool BWD, bool VEC, bool PROJ, typename E>
 __global__ void __launch_bounds__(SEGL_THREADS, 2)
-seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
+seg_local_kernel(const E *__restrict__ u, const E *__restrict__ dt,
                  const float *__restrict__ aneg, const float *__restrict__ row,
                  float *__restrict__ vout, float *__restrict__ pout,
                  int T, int D, int N, int L, int s_first, int bplanes, int splanes,
@@ -56,7 +57,9 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
     Proj pj = pj_in;                 // the prologue is compiled in only where it is used
     pj.on = PROJ;
     using S = SegLocalShape<G>;
-    constexpr int DPB = S::DPB, NPAD = S::NPAD, ROWF = S::ROWF, TT = SEGL_TT;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = SEGL_TT;
+    constexpr int CHF = TileRow<2, DPB, E>::CHF;           // floats of u, dt per step
+    constexpr int ROWF = CHF + NPAD;                       // <= S::ROWF
     extern __shared__ __align__(16) float smem[];
     const int tid = threadIdx.x;
     const int g = tid & (G - 1);
@@ -77,13 +80,13 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
         nan2[0] = f2(-a4.x * MMS_LOG2E, -a4.y * MMS_LOG2E);
         nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
-    const float *ub = u + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
+    const E *ub = u + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *rb = row + (size_t)b * T * N;
     // k-th tile in processing order (descending for the backward)
     auto tstart = [&](int k) { return BWD ? tb + (ntiles - 1 - k) * TT : tb + k * TT; };
     auto stage = [&](int buf, int k) {
         const int t0 = tstart(k);
-        stage_tile<2, 1, DPB, NPAD, TT, SEGL_THREADS, VEC>(smem + buf * TT * ROWF, ub, dtb, dtb,
+        stage_tile<2, 1, DPB, NPAD, TT, SEGL_THREADS, VEC, E>(smem + buf * TT * ROWF, ub, dtb, dtb,
                                                            rb, rb, t0, min(TT, te - t0), d0, D,
                                                            N, tid);
     };
@@ -110,10 +113,11 @@ seg_local_kernel(const float *__restrict__ u, const float *__restrict__ dt,
             // (with the prologue, dt = 0 must be kept there rather than mapped)
             const int j = BWD ? TT - 1 - jj : jj;
             const float *r = tile + j * ROWF;
-            const float uv = r[c];
-            float dtv = r[DPB + c];
+            const E *re = reinterpret_cast<const E *>(r);
+            const float uv = to_f(re[c]);
+            float dtv = to_f(re[DPB + c]);
             if (pj.on) dtv = tk + j < te ? fmaf(pj.range, sigmoid_fast(dtv), pj.lo) : 0.f;
-            const float4 R = *reinterpret_cast<const float4 *>(r + 2 * DPB + 4 * g);
+            const float4 R = *reinterpret_cast<const float4 *>(r + CHF + 4 * g);
             const float2 dt2 = f2(dtv, dtv);
             const float2 a0 = ex2x2(mul2(dt2, nan2[0])), a1 = ex2x2(mul2(dt2, nan2[1]));
             sdt += dtv;
@@ -181,15 +185,15 @@ __global__ void seg_combine_bwd_kernel(float *__restrict__ E, const float *__res
     }
 }
 
-template <int G, bool BWD, bool VEC, bool PROJ>
+template <int G, bool BWD, bool VEC, bool PROJ, typename E = float>
 static cudaError_t launch_local_gvp(const SegLocalArgs &a, cudaStream_t stream)
 {
     using S = SegLocalShape<G>;
-    cudaError_t e = smem_opt_in<seg_local_kernel<G, BWD, VEC, PROJ>>(S::SMEM);
+    cudaError_t e = smem_opt_in<seg_local_kernel<G, BWD, VEC, PROJ, E>>(S::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.nseg, a.Bt);
-    seg_local_kernel<G, BWD, VEC, PROJ><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
-        a.u, a.dt, a.aneg, a.row, a.vout, a.pout, a.T, a.D, a.N, a.L, a.s_first, a.bplanes,
+    seg_local_kernel<G, BWD, VEC, PROJ, E><<<grid, SEGL_THREADS, S::SMEM, stream>>>(
+        reinterpret_cast<const E *>(a.u), reinterpret_cast<const E *>(a.dt), a.aneg, a.row, a.vout, a.pout, a.T, a.D, a.N, a.L, a.s_first, a.bplanes,
         a.splanes, a.voff, a.poff, a.proj);
     return cudaGetLastError();
 }
@@ -212,6 +216,13 @@ static cudaError_t launch_local_g(const SegLocalArgs &a, bool backward, cudaStre
 
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream)
 {
+    if (a.bf16) {
+        // bf16 u, dt: the 9..16-state shapes of the bf16 entry points, 16-byte staging
+        if (groups_for(a.N) != 4 || !vec_ok(a.D, a.u, a.dt) || a.D % 8 != 0 || a.proj.on)
+            return cudaErrorInvalidValue;
+        return backward ? launch_local_gvp<4, true, true, false, __nv_bfloat16>(a, stream)
+                        : launch_local_gvp<4, false, true, false, __nv_bfloat16>(a, stream);
+    }
     switch (groups_for(a.N)) {
     case 1: return launch_local_g<1>(a, backward, stream);
     case 2: return launch_local_g<2>(a, backward, stream);

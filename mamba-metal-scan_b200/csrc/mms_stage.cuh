@@ -53,33 +53,44 @@ __device__ __forceinline__ void fence_async_smem() {
 
 // Copy `rows` consecutive time steps [t0, t0+rows) of NARR channel arrays
 // (each (T, D) row-major, already offset to the batch row) and of NBC state
-// arrays (each (T, N)) into a tile laid out per step as
+// arrays (each (T, N), fp32) into a tile laid out per step as
 //     [arr0[DPB] arr1[DPB] ... arr{NARR-1}[DPB] bc0[NPAD] bc1[NPAD] ...]
-// (ROWF floats per step). Steps >= nvalid, channels >= D - d0 and states >= N
-// are zero-filled. VEC selects 16-byte copies for the channel arrays, which
-// needs D % 4 == 0 and 16-byte aligned arrays (checked by the host).
+// (ROWF floats per step). The channel arrays keep their storage type E
+// (float, or bf16 whose NARR*DPB elements then take NARR*DPB/2 floats of the
+// row). Steps >= nvalid, channels >= D - d0 and states >= N are zero-filled.
+// VEC selects 16-byte copies for the channel arrays, which needs every row
+// 16-byte aligned (D a multiple of 16/sizeof(E), aligned arrays; checked by
+// the host); bf16 arrays are always staged that way.
 //
 // The arrays are passed as separate pointers (a2 unused when NARR == 2) and
 // picked by value, so no pointer table lands in local memory.
-template <int NARR, int NBC, int DPB, int NPAD, int ROWS, int NTHREADS, bool VEC>
-__device__ __forceinline__ void stage_tile(float *tile, const float *a0, const float *a1,
-                                           const float *a2, const float *b0, const float *b1,
+template <int NARR, int DPB, typename E>
+struct TileRow {
+    static constexpr int CHF = NARR * DPB * (int)sizeof(E) / 4;   // floats of the channel arrays
+};
+
+template <int NARR, int NBC, int DPB, int NPAD, int ROWS, int NTHREADS, bool VEC, typename E = float>
+__device__ __forceinline__ void stage_tile(float *tile, const E *a0, const E *a1, const E *a2,
+                                           const float *b0, const float *b1,
                                            int t0, int nvalid, int d0, int D, int N, int tid)
 {
+    static_assert(VEC || sizeof(E) == 4, "bf16 channel arrays are staged in 16-byte pieces");
     auto arr = [&](int a) { return a == 0 ? a0 : (a == 1 || NARR == 2) ? a1 : a2; };
     auto bc = [&](int a) { return a == 0 || NBC == 1 ? b0 : b1; };
-    constexpr int ROWF = NARR * DPB + NBC * NPAD;
+    constexpr int CHF = TileRow<NARR, DPB, E>::CHF;
+    constexpr int ROWF = CHF + NBC * NPAD;
     const int dleft = D - d0;
     if constexpr (VEC) {
-        constexpr int QD = DPB / 4;                    // float4 per channel row
+        constexpr int EPV = 16 / (int)sizeof(E);         // elements per 16-byte copy
+        constexpr int QD = DPB / EPV;                    // copies per channel row
         constexpr int TOT = NARR * ROWS * QD;
         for (int k = tid; k < TOT; k += NTHREADS) {
             const int a = k / (ROWS * QD);
             const int r = (k / QD) % ROWS;
             const int q = k % QD;
-            const bool ok = r < nvalid && 4 * q < dleft;
-            const float *src = ok ? arr(a) + (size_t)(t0 + r) * D + d0 + 4 * q : arr(a);
-            cp16(tile + r * ROWF + a * DPB + 4 * q, src, ok);
+            const bool ok = r < nvalid && EPV * q < dleft;
+            const E *src = ok ? arr(a) + (size_t)(t0 + r) * D + d0 + EPV * q : arr(a);
+            cp16(reinterpret_cast<E *>(tile + r * ROWF) + a * DPB + EPV * q, src, ok);
         }
     } else {
         constexpr int TOT = NARR * ROWS * DPB;
@@ -100,7 +111,7 @@ __device__ __forceinline__ void stage_tile(float *tile, const float *a0, const f
         const int q = k % QN;
         const bool ok = r < nvalid && 4 * q < N;
         const float *src = ok ? bc(a) + (size_t)(t0 + r) * N + 4 * q : bc(a);
-        cp16(tile + r * ROWF + NARR * DPB + a * NPAD + 4 * q, src, ok);
+        cp16(tile + r * ROWF + CHF + a * NPAD + 4 * q, src, ok);
     }
 }
 

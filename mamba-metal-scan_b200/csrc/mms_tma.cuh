@@ -62,19 +62,21 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tma_encoder()
     return fn;
 }
 
-// fp32 tile map over a row-major array whose innermost `rank` dims are `dim`
-// (dim[0] contiguous), box `box`; out-of-range elements load as zeros.
+// Tile map over a row-major array of fp32 (elem 4) or bf16 (elem 2) whose
+// innermost `rank` dims are `dim` (dim[0] contiguous), box `box`;
+// out-of-range elements load as zeros.
 inline bool tma_encode(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap *m, const void *base, int rank,
-            const cuuint64_t *dim, const cuuint32_t *box)
+            const cuuint64_t *dim, const cuuint32_t *box, int elem = 4)
 {
     cuuint64_t stride[4];
-    cuuint64_t s = 4;
+    cuuint64_t s = (cuuint64_t)elem;
     for (int i = 0; i + 1 < rank; ++i) {
         s *= dim[i];
         stride[i] = s;
     }
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void *>(base), dim, stride, box,
+    const CUtensorMapDataType ty = elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    return fn(m, ty, rank, const_cast<void *>(base), dim, stride, box,
               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

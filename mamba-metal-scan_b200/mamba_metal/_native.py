@@ -23,6 +23,7 @@ MMS_ERR_MISALIGNED = 4
 MMS_ERR_CUDA = 5
 MMS_ERR_TOO_LARGE = 6
 MMS_ERR_TIMEOUT = 7
+MMS_ERR_UNSUPPORTED_BF16 = 8
 
 # Every symbol include/mms_scan.h declares, with its ctypes signature.
 _P = ctypes.c_void_p
@@ -43,6 +44,8 @@ SIGNATURES = {
     "mms_fwd_proj": ([_P] * 5 + [ctypes.c_float] * 2 + [_P] * 2 + [_I] * 5 + [_P], _I),
     "mms_bwd_proj": ([_P] * 7 + [ctypes.c_float] * 2 + [_P] * 6 + [ctypes.c_size_t] + [_I] * 5
                      + [_P], _I),
+    "mms_fwd_bf16": ([_P] * 7 + [_I] * 5 + [_P], _I),
+    "mms_bwd_bf16": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
 }
 
 _lib = None
@@ -143,6 +146,42 @@ def bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None, proj=None
                               _ptr(workspace), workspace.numel(),
                               bt, t_len, d, n, chunk, _stream(x.device))
         _check(rc, "mms_bwd_proj")
+    return dx, ddt, daneg, db, dc
+
+
+def fwd_bf16(x, dt, aneg, b_in, c_in, chunk: int):
+    """mms_fwd_bf16: x, dt bf16 (B,T,D), Aneg/B/C fp32; returns y bf16 (B,T,D)
+    and the fp32 ckpt (B, ceil(T/chunk), D, N)."""
+    lib = load()
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    nchunk = (t_len + chunk - 1) // chunk
+    y = torch.empty(bt, t_len, d, device=x.device, dtype=torch.bfloat16)
+    ckpt = torch.empty(bt, nchunk, d, n, device=x.device, dtype=torch.float32)
+    rc = lib.mms_fwd_bf16(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(y),
+                          _ptr(ckpt), bt, t_len, d, n, chunk, _stream(x.device))
+    _check(rc, "mms_fwd_bf16")
+    return y, ckpt
+
+
+def bwd_bf16(x, dt, aneg, b_in, c_in, dy, ckpt, chunk: int, workspace=None):
+    """mms_bwd_bf16: (dx, ddt) bf16 and (dAneg, dB, dC) fp32."""
+    lib = load()
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    dx = torch.empty_like(x)
+    ddt = torch.empty_like(dt)
+    daneg = torch.empty_like(aneg)
+    db = torch.empty_like(b_in)
+    dc = torch.empty_like(c_in)
+    ws_bytes = bwd_workspace_size(bt, t_len, d, n, chunk)
+    if workspace is None or workspace.numel() < ws_bytes:
+        workspace = torch.empty(max(ws_bytes, 1), device=x.device, dtype=torch.uint8)
+    rc = lib.mms_bwd_bf16(_ptr(x), _ptr(dt), _ptr(aneg), _ptr(b_in), _ptr(c_in), _ptr(dy),
+                          _ptr(ckpt), _ptr(dx), _ptr(ddt), _ptr(daneg), _ptr(db), _ptr(dc),
+                          _ptr(workspace), workspace.numel(),
+                          bt, t_len, d, n, chunk, _stream(x.device))
+    _check(rc, "mms_bwd_bf16")
     return dx, ddt, daneg, db, dc
 
 

@@ -277,6 +277,98 @@ def selective_scan_proj(x: torch.Tensor, dt_logit: torch.Tensor, a_param: torch.
     return None
 
 
+# ---------------------------------------------------- bf16 storage (f4)
+
+BF16_STATES = (12, 16)
+
+
+def _validate_bf16(x, dt, aneg, b_in, c_in, chunk: int):
+    tensors = (x, dt, aneg, b_in, c_in)
+    if not all(t.is_cuda for t in tensors) or len({t.device for t in tensors}) != 1:
+        raise RuntimeError("selective_scan_bf16 needs every input on the same CUDA device; saw "
+                           + ", ".join(str(t.device) for t in tensors))
+    if x.dtype != torch.bfloat16 or dt.dtype != torch.bfloat16:
+        raise RuntimeError(f"selective_scan_bf16 takes bf16 x and dt; got {x.dtype}, {dt.dtype}")
+    if not all(t.is_floating_point() for t in (aneg, b_in, c_in)):
+        raise RuntimeError("Aneg, B and C must be floating point")
+    if x.dim() != 3 or dt.shape != x.shape or aneg.dim() != 2:
+        raise ValueError(f"bad shapes: x {tuple(x.shape)}, dt {tuple(dt.shape)}, "
+                         f"Aneg {tuple(aneg.shape)}")
+    bt, t_len, d = x.shape
+    n = aneg.shape[1]
+    if aneg.shape[0] != d or b_in.shape != (bt, t_len, n) or c_in.shape != (bt, t_len, n):
+        raise ValueError(f"Aneg {tuple(aneg.shape)}, B {tuple(b_in.shape)}, C {tuple(c_in.shape)} "
+                         f"do not match x {tuple(x.shape)}")
+    if n not in BF16_STATES:
+        raise ValueError(f"the bf16 scan supports d_state {BF16_STATES}; got {n}")
+    if d % 8 != 0:
+        raise ValueError(f"the bf16 scan needs d_inner % 8 == 0; got {d}")
+    if chunk != 8:
+        raise ValueError(f"the bf16 scan uses checkpoint stride 8; got chunk={chunk}")
+
+
+class SelectiveScanBF16CUDA(torch.autograd.Function):
+    """selective_scan_bf16(x, dt, Aneg, B, C) -> y (bf16), forward and backward.
+
+    x, dt and y (and dy, dx, ddt) are stored as bf16; Aneg, B, C are used as
+    fp32, as are the checkpoints and all arithmetic (mms_fwd_bf16 /
+    mms_bwd_bf16). Gradients come back in each input's own dtype.
+    """
+
+    @staticmethod
+    def forward(ctx, x, dt, aneg, b_in, c_in, chunk=SSM_CHUNK, return_state=False):
+        chunk = int(chunk)
+        _validate_bf16(x, dt, aneg, b_in, c_in, chunk)
+        ctx.dtypes = (aneg.dtype, b_in.dtype, c_in.dtype)
+        bt, t_len, d = x.shape
+        n = aneg.shape[1]
+        x = _aligned(x, 16)
+        dt = _aligned(dt, 16)
+        aneg = _aligned(aneg.float(), 16)
+        b_in = _aligned(b_in.float(), 16)
+        c_in = _aligned(c_in.float(), 16)
+        with torch.cuda.device(x.device):
+            if bt == 0 or t_len == 0 or d == 0:
+                y = x.new_zeros(bt, t_len, d)
+                ckpt = aneg.new_zeros(bt, 0, d, n)
+            else:
+                y, ckpt = _native.fwd_bf16(x, dt, aneg, b_in, c_in, chunk)
+        ctx.save_for_backward(x, dt, aneg, b_in, c_in, ckpt)
+        ctx.chunk = chunk
+        if return_state:
+            state = ckpt[:, -1].detach() if ckpt.shape[1] else aneg.new_zeros(bt, d, n)
+            return y, state
+        return y
+
+    @staticmethod
+    def backward(ctx, *grads):
+        dy = grads[0]
+        x, dt, aneg, b_in, c_in, ckpt = ctx.saved_tensors
+        ta, tb, tc = ctx.dtypes
+        bt, t_len, d = x.shape
+        if dy is None or bt == 0 or t_len == 0 or d == 0:
+            return (torch.zeros_like(x), torch.zeros_like(dt), torch.zeros_like(aneg, dtype=ta),
+                    torch.zeros_like(b_in, dtype=tb), torch.zeros_like(c_in, dtype=tc), None, None)
+        dy = _aligned(dy.to(torch.bfloat16), 16)
+        with torch.cuda.device(x.device):
+            dx, ddt, daneg, db, dc = _native.bwd_bf16(x, dt, aneg, b_in, c_in, dy, ckpt, ctx.chunk)
+        return dx, ddt, daneg.to(ta), db.to(tb), dc.to(tc), None, None
+
+
+def selective_scan_bf16(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
+                        b_in: torch.Tensor, c_in: torch.Tensor,
+                        chunk: int = SSM_CHUNK, return_state: bool = False):
+    """The scan with bf16 x, dt and y (no counterpart in the fp32-only reference).
+
+    Same recurrence and autograd contract as `selective_scan`; x and dt are
+    bf16 CUDA tensors, Aneg, B and C any float dtype (used as fp32), y is
+    bf16. Covers d_state 12 or 16, d_inner a multiple of 8, chunk 8 (the
+    shapes of the whole-state forward and the 8-state backward kernels);
+    other shapes raise ValueError.
+    """
+    return SelectiveScanBF16CUDA.apply(x, dt, aneg, b_in, c_in, chunk, return_state)
+
+
 # ------------------------------------------------------ gate epilogue (f3)
 
 def gate_ref(y, z, d_skip):

@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from _inputs import inputs
-from mamba_metal import _native, selective_scan, selective_scan_ref
+from mamba_metal import _native, selective_scan, selective_scan_bf16, selective_scan_ref
 from mamba_metal.scan import SelectiveScanCUDA
 
 REPO = Path(__file__).resolve().parents[1]
@@ -37,8 +37,8 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _native.load()
-    assert lib.mms_abi_version() == 103
-    for rc in range(8):
+    assert lib.mms_abi_version() == 104
+    for rc in range(9):
         assert _native.status_string(rc) != "unknown status"
     assert _native.status_string(99) == "unknown status"
 
@@ -64,6 +64,34 @@ def test_bad_arguments_return_status_without_launching():
     assert lib.mms_bwd(*bargs, ctypes.c_void_p(0x20010), need, 2, 8, 16, 16, 64, null) \
         == _native.MMS_ERR_MISALIGNED
     assert lib.mms_bwd_workspace_size(2, 8, 16, 6, 64) == 0
+
+
+def test_bf16_entry_points_check_their_shapes_first():
+    """bf16 storage covers 8 < N <= 16, D % 8 == 0, K == 8 (forward K >= 8)."""
+    lib = _native.load()
+    null = None
+    fake = [ctypes.c_void_p(0x10000)] * 7
+    unsup = _native.MMS_ERR_UNSUPPORTED_BF16
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 8, 8, null) == unsup       # N = 8
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 20, 8, null) == unsup      # N = 20
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 12, 16, 8, null) == unsup      # D % 8
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 16, 4, null) == unsup      # K < 8
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 6, 8, null) == _native.MMS_ERR_UNSUPPORTED_N
+    assert lib.mms_fwd_bf16(*([null] * 7), 2, 8, 16, 16, 8, null) == _native.MMS_ERR_INVALID_ARG
+    # bf16 arrays need 16-byte alignment (fp32 ones: 16 as before)
+    odd = [ctypes.c_void_p(0x10008)] + [ctypes.c_void_p(0x10000)] * 6
+    assert lib.mms_fwd_bf16(*odd, 2, 8, 16, 16, 8, null) == _native.MMS_ERR_MISALIGNED
+    bargs = [ctypes.c_void_p(0x10000)] * 12
+    need = lib.mms_bwd_workspace_size(2, 8, 16, 16, 8)
+    ws = ctypes.c_void_p(0x20000)
+    assert lib.mms_bwd_bf16(*bargs, ws, need, 2, 8, 16, 16, 16, null) == unsup   # K != 8
+    assert lib.mms_bwd_bf16(*bargs, ws, need - 1, 2, 8, 16, 16, 8, null) == _native.MMS_ERR_WORKSPACE
+
+
+def test_bf16_scan_needs_cuda_tensors():
+    x, dt, aneg, b_in, c_in, _ = inputs(1, 8, 16, 16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        selective_scan_bf16(x.bfloat16(), dt.bfloat16(), aneg, b_in, c_in)
 
 
 def test_workspace_grows_with_long_chunks():
