@@ -52,8 +52,8 @@ extern "C" {
                                       MMS_NOALLOC_SCRATCH_BYTES                          */
 #define MMS_ERR_TIMEOUT 7          /* a kernel gave up waiting for its own staged copies
                                       (reported by mms_device_status)                    */
-#define MMS_ERR_UNSUPPORTED_BF16 8 /* the bf16 entry points need 8 < N <= 16, D % 8 == 0
-                                      and K == 8 (forward: K >= 8)                       */
+#define MMS_ERR_UNSUPPORTED_BF16 8 /* the bf16 entry points need D % 8 == 0, and K == 8
+                                      for the backward                                   */
 
 /* Version of the ABI in this header (major * 100 + minor). */
 #define MMS_ABI_VERSION 104
@@ -186,9 +186,10 @@ int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ld
  * and exponential is computed in float32 as in mms_fwd / mms_bwd. Outputs
  * are rounded to bf16 once, at the store. Halves the bytes of the six
  * arrays that dominate the traffic.
- * Shapes: 8 < N <= 16 (N = 12 or 16), D % 8 == 0, K == 8 for the backward
- * and K >= 8 for the forward; otherwise MMS_ERR_UNSUPPORTED_BF16. The bf16
- * arrays must be 16-byte aligned. Workspace as mms_bwd (same size function).
+ * Shapes: every N of mms_fwd / mms_bwd; D % 8 == 0, and K == 8 for the
+ * backward (any K for the forward); otherwise MMS_ERR_UNSUPPORTED_BF16. The
+ * bf16 arrays must be 16-byte aligned. Workspace as mms_bwd (same size
+ * function).
  * No counterpart in the reference, which is float32-only
  * (mamba_metal/scan.py:350-354).
  */

@@ -59,11 +59,11 @@ int bwd_impl(const float *x, const float *dt, const float *aneg, const float *B,
                                                                                  : MMS_ERR_CUDA;
 }
 
-// Shapes the bf16 entry points cover (the whole-state forward and the
-// 8-state backward, both staged by TMA in 16-byte rows).
-int check_bf16(int N, int D, int K, bool backward)
+// Shapes the bf16 entry points cover: bf16 rows staged in 16-byte pieces
+// (D % 8 == 0); the backward at checkpoint stride 8 (its 8-step kernels).
+int check_bf16(int D, int K, bool backward)
 {
-    if (N <= 8 || N > 16 || D % 8 != 0 || (backward ? K != 8 : K < 8)) return MMS_ERR_UNSUPPORTED_BF16;
+    if (D % 8 != 0 || (backward && K != 8)) return MMS_ERR_UNSUPPORTED_BF16;
     return MMS_OK;
 }
 
@@ -95,7 +95,7 @@ const char *mms_status_string(int status)
     case MMS_ERR_CUDA: return "CUDA launch failed";
     case MMS_ERR_TIMEOUT: return "a kernel timed out waiting for its staged copies (results invalid)";
     case MMS_ERR_UNSUPPORTED_BF16:
-        return "bf16 scan needs 8 < N <= 16, D % 8 == 0 and K == 8 (forward: K >= 8)";
+        return "bf16 scan needs D % 8 == 0 (and K == 8 for the backward)";
     case MMS_ERR_TOO_LARGE:
         return "shape needs more workspace than mms_bwd_noalloc's static scratch "
                "(MMS_NOALLOC_SCRATCH_BYTES = 16 MiB); use mms_bwd with a caller workspace";
@@ -203,7 +203,7 @@ int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
 {
     int rc = check_shape(Bt, T, D, N, K);
     if (rc) return rc;
-    if ((rc = check_bf16(N, D, K, false))) return rc;
+    if ((rc = check_bf16(D, K, false))) return rc;
     if (!x || !dt || !aneg || !B || !C || !y || !ckpt) return MMS_ERR_INVALID_ARG;
     if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
         !aligned(x, 16) || !aligned(dt, 16) || !aligned(y, 16))
@@ -220,7 +220,7 @@ int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
 {
     int rc = check_shape(Bt, T, D, N, K);
     if (rc) return rc;
-    if ((rc = check_bf16(N, D, K, true))) return rc;
+    if ((rc = check_bf16(D, K, true))) return rc;
     if (!x || !dt || !aneg || !B || !C || !dy || !ckpt || !dx || !ddt || !daneg || !dB || !dC)
         return MMS_ERR_INVALID_ARG;
     if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||

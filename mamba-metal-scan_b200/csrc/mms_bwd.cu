@@ -144,18 +144,23 @@ __device__ __forceinline__ float2 shfl2(float2 v, int m) {
     return f2(__shfl_xor_sync(0xffffffffu, v.x, m), __shfl_xor_sync(0xffffffffu, v.y, m));
 }
 
-// Rewrite a natural tile into the compute layouts (see the file comment).
-template <int G>
+// Rewrite a natural tile into the compute layouts (see the file comment); x,
+// dt, dy are widened from their storage type E to fp32 here.
+template <int G, typename E = float>
 __device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int tid, const Proj &pj)
 {
     using S = BwdShape<G>;
-    constexpr int DPB = S::DPB, NPAD = S::NPAD, NROWF = S::NROWF, QF = S::QF, PF = S::PF;
+    constexpr int DPB = S::DPB, NPAD = S::NPAD, QF = S::QF, PF = S::PF;
+    constexpr int CHF = TileRow<3, DPB, E>::CHF;           // floats of x, dt, dy per step
+    constexpr int NROWF = CHF + 2 * NPAD;                  // staged row (floats)
+    constexpr int RSTR = NROWF * 4 / (int)sizeof(E);       // the same in elements of E
     constexpr int NQ = GRP / 4;
     for (int e = tid; e < 3 * NQ * DPB; e += BWD_THREADS) {
         const int a = e / (NQ * DPB), rem = e % (NQ * DPB);
         const int q = rem / DPB, cc = rem % DPB;
-        const float *src = nat + (4 * q) * NROWF + a * DPB + cc;
-        float4 v4 = make_float4(src[0], src[NROWF], src[2 * NROWF], src[3 * NROWF]);
+        const E *src = reinterpret_cast<const E *>(nat + (4 * q) * NROWF) + a * DPB + cc;
+        float4 v4 = make_float4(to_f(src[0]), to_f(src[RSTR]), to_f(src[2 * RSTR]),
+                                to_f(src[3 * RSTR]));
         if (pj.on && a == 1)
             v4 = make_float4(fmaf(pj.range, sigmoid_fast(v4.x), pj.lo), fmaf(pj.range, sigmoid_fast(v4.y), pj.lo),
                              fmaf(pj.range, sigmoid_fast(v4.z), pj.lo), fmaf(pj.range, sigmoid_fast(v4.w), pj.lo));
@@ -168,7 +173,7 @@ __device__ __forceinline__ void rewrite_tile(const float *nat, float *der, int t
         const int i = (e / (NQ4 * S::NPERM)) % GRP;
         const int a = e / (NQ4 * S::NPERM * GRP);
         const int tau = S::NPERM == 4 ? pi : 2 * pi;
-        const float *src = nat + i * NROWF + 3 * DPB + a * NPAD + 4 * q4;
+        const float *src = nat + i * NROWF + CHF + a * NPAD + 4 * q4;
         *reinterpret_cast<float4 *>(der + 3 * QF + a * PF + (i * S::NPERM + pi) * NPAD + 4 * q4) =
             make_float4(src[0 ^ tau], src[1 ^ tau], src[2 ^ tau], src[3 ^ tau]);
     }
@@ -287,13 +292,13 @@ struct Adjoint {
 #define MMS_WALK_KEEP_A 0
 #endif
 
-template <int G, bool FULL>
+template <int G, bool FULL, typename E = float>
 __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&hb)[2],
                                            const Lane<G> &L, Adjoint &A, int nv,
-                                           float *dxo, float *ddto, int D, float *sd,
+                                           E *dxo, E *ddto, int D, float *sd,
                                            const Proj &pj)
 {
-    float *outp = L.n_ddt ? ddto : dxo;
+    E *outp = L.n_ddt ? ddto : dxo;
     using S = BwdShape<G>;
     constexpr int NPAD = S::NPAD, NV2 = S::NV2;
     // Rebuild: the states of the group's steps (and, when kept, their decays).
@@ -366,11 +371,11 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
                     transposed_reduce<2, G / 2, 1>(vn, L.lane, fn);
                     // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
                     if (pj.on && L.n_ddt) vn[0] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
-                    if (L.n_writer) outp[(size_t)i * D] = vn[0];
+                    if (L.n_writer) outp[(size_t)i * D] = from_f<E>(vn[0]);
                 } else if (L.n_writer) {
                     if (pj.on) vn[1] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
-                    dxo[(size_t)i * D] = vn[0];
-                    ddto[(size_t)i * D] = vn[1];
+                    dxo[(size_t)i * D] = from_f<E>(vn[0]);
+                    ddto[(size_t)i * D] = from_f<E>(vn[1]);
                 }
             }
             // dB|dC butterfly across the warp's channels
@@ -598,13 +603,14 @@ bwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 // Backward for checkpoint stride K == GRP: every chunk is one group whose
 // entry state is the forward's checkpoint, so there is no recompute pass and
 // no slot storage; groups are simply chunks nchunk-1 .. 0.
-template <int G, bool VEC, bool PROJ>
+// E: storage type of x, dt, dy, dx, ddt (float or bf16).
+template <int G, bool VEC, bool PROJ, typename E>
 __global__ void __launch_bounds__(BWD_THREADS, MMS_BWD_K8_MINB)
-bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
+bwd_kernel_k8(const E *__restrict__ x, const E *__restrict__ dt,
               const float *__restrict__ aneg, const float *__restrict__ Bm,
-              const float *__restrict__ Cm, const float *__restrict__ dy,
-              const float *__restrict__ ckpt, float *__restrict__ dx,
-              float *__restrict__ ddt, float *__restrict__ part_bc,
+              const float *__restrict__ Cm, const E *__restrict__ dy,
+              const float *__restrict__ ckpt, E *__restrict__ dx,
+              E *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
               int T, int D, int N, int nblk, int cps, Proj pj_in)
 {
@@ -623,14 +629,14 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     const int nchunk = (T + GRP - 1) / GRP;
     const size_t plane = (size_t)D * N;
     const size_t rowD = (size_t)L.b * T * D;
-    const float *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
+    const E *xb = x + rowD, *dtb = dt + rowD, *dyb = dy + rowD;
     const float *Bb = Bm + (size_t)L.b * T * N, *Cb = Cm + (size_t)L.b * T * N;
     const float *ckb = ckpt + (size_t)L.b * nchunk * plane;
     float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
 
     // Stage group c: its inputs and the checkpoint it starts from (zeros for c == 0).
     auto stage = [&](int buf, int c) {
-        stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC>(
+        stage_tile<3, 2, DPB, NPAD, GRP, BWD_THREADS, VEC, E>(
             nat + buf * S::NATF, xb, dtb, dyb, Bb, Cb, c * GRP, min(GRP, T - c * GRP),
             L.d0, D, N, tid);
         constexpr int QN = NPAD / 4;
@@ -660,7 +666,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
     }
     cp_wait<NAT_BUFS - 1>();
     __syncthreads();
-    rewrite_tile<G>(nat, der, tid, pj);
+    rewrite_tile<G, E>(nat, der, tid, pj);
     float2 hnext[2];                                   // state entering the current group
     entry(hnext, 0);
 
@@ -677,7 +683,7 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const float2 hb[2] = {hnext[0], hnext[1]};
         if (c - 1 >= clo) {                            // group it+1: rewrite, take its entry state
             const int nb = (it + 1) % NAT_BUFS;
-            rewrite_tile<G>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid, pj);
+            rewrite_tile<G, E>(nat + nb * S::NATF, der + ((it + 1) % DER_BUFS) * S::DERF, tid, pj);
             entry(hnext, nb);
         }
         if (c - NAT_BUFS >= clo) stage((it + NAT_BUFS) % NAT_BUFS, c - NAT_BUFS);
@@ -687,10 +693,10 @@ bwd_kernel_k8(const float *__restrict__ x, const float *__restrict__ dt,
         const TileView<G> v(dtile, L.c, L.g, L.pidx);
         const int t0 = c * GRP;
         const int nv = min(GRP, T - t0);
-        float *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
+        E *dxo = dx + rowD + (size_t)t0 * D + L.d, *ddto = ddt + rowD + (size_t)t0 * D + L.d;
         float *sdb = sd + (it & 1) * S::SDF;
-        if (nv == GRP) walk_group<G, true>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
-        else walk_group<G, false>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
+        if (nv == GRP) walk_group<G, true, E>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
+        else walk_group<G, false, E>(v, hb, L, A, nv, dxo, ddto, D, sdb, pj);
     }
     cp_wait<0>();
     __syncthreads();
@@ -760,7 +766,7 @@ BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K)
     return w;
 }
 
-template <int G, bool VEC, bool PROJ>
+template <int G, bool VEC, bool PROJ, typename E = float>
 static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaStream_t stream)
 {
     using S = BwdShape<G>;
@@ -782,14 +788,18 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
-    if (a.bf16 || (MMS_BWD_W8 && G == 4 && bwd_w8_applies(a.N, a.K))) {
+    if (G == 4 && bwd_w8_applies(a.N, a.K) && (MMS_BWD_W8 || a.bf16)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
-        e = smem_opt_in<bwd_kernel_k8<G, VEC, PROJ>>(S::SMEM_K8);
+        e = smem_opt_in<bwd_kernel_k8<G, VEC, PROJ, E>>(S::SMEM_K8);
         if (e != cudaSuccess) return e;
-        bwd_kernel_k8<G, VEC, PROJ><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
-            a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, seg_e,
-            a.T, a.D, a.N, w.nblk, sp.cps, a.proj);
+        auto cE = [](const float *p) { return reinterpret_cast<const E *>(p); };
+        auto mE = [](float *p) { return reinterpret_cast<E *>(p); };
+        bwd_kernel_k8<G, VEC, PROJ, E><<<grid, BWD_THREADS, S::SMEM_K8, stream>>>(
+            cE(a.x), cE(a.dt), a.aneg, a.B, a.C, cE(a.dy), a.ckpt, mE(a.dx), mE(a.ddt), part_bc,
+            part_a, seg_e, a.T, a.D, a.N, w.nblk, sp.cps, a.proj);
+    } else if constexpr (sizeof(E) != 4) {
+        return cudaErrorInvalidValue;                  // bf16 storage: stride 8 only
     } else {
         e = smem_opt_in<bwd_kernel<G, VEC, PROJ>>(S::SMEM);
         if (e != cudaSuccess) return e;
@@ -826,9 +836,20 @@ cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream)
 {
     const BwdWorkspace w = bwd_workspace_layout(a.Bt, a.T, a.D, a.N, a.K);
     if (a.bf16) {
-        // bf16 channel arrays: only the 8-state backward reads them (8 < N <= 16, K == 8)
-        if (!bwd_w8_applies(a.N, a.K)) return cudaErrorInvalidValue;
-        return launch_bwd_gvp<4, true, false>(a, w, stream);
+        // bf16 channel arrays: the stride-8 backwards (8-state for 8 < N <= 16,
+        // else 4-state), 16-byte staging
+        if (a.K != GRP || a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt, a.dy) ||
+            !vec_ok(a.D, a.dx, a.ddt))
+            return cudaErrorInvalidValue;
+        using BF = __nv_bfloat16;
+        switch (groups_for(a.N)) {
+        case 1: return launch_bwd_gvp<1, true, false, BF>(a, w, stream);
+        case 2: return launch_bwd_gvp<2, true, false, BF>(a, w, stream);
+        case 4: return launch_bwd_gvp<4, true, false, BF>(a, w, stream);
+        case 8: return launch_bwd_gvp<8, true, false, BF>(a, w, stream);
+        case 16: return launch_bwd_gvp<16, true, false, BF>(a, w, stream);
+        default: return cudaErrorInvalidValue;
+        }
     }
     switch (groups_for(a.N)) {
     case 1: return launch_bwd_g<1>(a, w, stream);

@@ -38,17 +38,21 @@ struct FwdShape {
                                                     + (size_t)TT * DPB * G);
 };
 
-template <int G, bool VEC, bool PROJ>
+// E: storage type of x, dt and y (float or bf16; bf16 rows are staged in
+// 16-byte pieces, VEC).
+template <int G, bool VEC, bool PROJ, typename E>
 __global__ void __launch_bounds__(FWD_THREADS, 2)
-fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
+fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
            const float *__restrict__ aneg, const float *__restrict__ Bm,
-           const float *__restrict__ Cm, float *__restrict__ y,
+           const float *__restrict__ Cm, E *__restrict__ y,
            float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps, Proj pj_in)
 {
     Proj pj = pj_in;                 // the prologue is compiled in only where it is used
     pj.on = PROJ;
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
+    constexpr int CHF = TileRow<2, DPB, E>::CHF;           // floats of x, dt per staged step
+    constexpr int RROW = CHF + 2 * NPAD;                   // staged step (floats), <= ROWF
     extern __shared__ __align__(128) float smem[];
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
     float *ys = smem + FWD_STAGES * TT * ROWF;             // [TT][DPB][G] partial y
@@ -75,10 +79,10 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         nan2[1] = f2(-a4.z * MMS_LOG2E, -a4.w * MMS_LOG2E);
     }
 
-    const float *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
+    const E *xb = x + (size_t)b * T * D, *dtb = dt + (size_t)b * T * D;
     const float *Bb = Bm + (size_t)b * T * N, *Cb = Cm + (size_t)b * T * N;
     float *ckb = ckpt + (size_t)b * nchunk * D * N + (size_t)d * N + 4 * g;
-    float *yb = y + (size_t)b * T * D;
+    E *yb = y + (size_t)b * T * D;
 
     // The state entering the segment: the checkpoint the segment combine left
     // at the end of the previous segment (zero for the first).
@@ -95,7 +99,7 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 #pragma unroll
     for (int s = 0; s < FWD_STAGES - 1; ++s) {
         if (s < ntiles)
-            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
+            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC, E>(tiles + s * TT * ROWF, xb, dtb, dtb, Bb, Cb,
                                                               tb + s * TT, min(TT, te - tb - s * TT),
                                                               d0, D, N, tid);
         cp_commit();
@@ -108,7 +112,7 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         __syncthreads();
         const int kn = k + FWD_STAGES - 1;
         if (kn < ntiles)
-            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC>(
+            stage_tile<2, 2, DPB, NPAD, TT, FWD_THREADS, VEC, E>(
                 tiles + (kn % FWD_STAGES) * TT * ROWF, xb, dtb, dtb, Bb, Cb, tb + kn * TT,
                 min(TT, te - tb - kn * TT), d0, D, N, tid);
         cp_commit();
@@ -117,13 +121,14 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
         const int t0 = tb + k * TT;
 #pragma unroll
         for (int j = 0; j < TT; ++j) {
-            const float *row = tile + j * ROWF;
+            const float *row = tile + j * RROW;
+            const E *re = reinterpret_cast<const E *>(row);
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = row[c];
-            float dtv = row[DPB + c];
+            const float xv = to_f(re[c]);
+            float dtv = to_f(re[DPB + c]);
             if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
-            const float4 Bv = *reinterpret_cast<const float4 *>(row + 2 * DPB + 4 * g);
-            const float4 Cv = *reinterpret_cast<const float4 *>(row + 2 * DPB + NPAD + 4 * g);
+            const float4 Bv = *reinterpret_cast<const float4 *>(row + CHF + 4 * g);
+            const float4 Cv = *reinterpret_cast<const float4 *>(row + CHF + NPAD + 4 * g);
             const float bx = dtv * xv;
             const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
             h[0] = fma2(ex2x2(mul2(dt2, nan2[0])), h[0], mul2(bx2, lo(Bv)));
@@ -153,7 +158,7 @@ fwd_kernel(const float *__restrict__ x, const float *__restrict__ dt,
 #pragma unroll
                 for (int q = 0; q < G; ++q) sum += src[q];
             }
-            if (t0 + j < te && d0 + cc < D) yb[(size_t)(t0 + j) * D + d0 + cc] = sum;
+            if (t0 + j < te && d0 + cc < D) yb[(size_t)(t0 + j) * D + d0 + cc] = from_f<E>(sum);
         }
     }
 }
@@ -540,11 +545,11 @@ int fwd_take_timeout()
     return v ? 1 : 0;
 }
 
-template <int G, bool VEC, bool PROJ>
+template <int G, bool VEC, bool PROJ, typename E = float>
 static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
 {
     using S = FwdShape<G>;
-    cudaError_t e = smem_opt_in<fwd_kernel<G, VEC, PROJ>>(S::SMEM);
+    cudaError_t e = smem_opt_in<fwd_kernel<G, VEC, PROJ, E>>(S::SMEM);
     if (e != cudaSuccess) return e;
     const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K);
     const int nchunk = (a.T + a.K - 1) / a.K;
@@ -559,8 +564,9 @@ static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
             return e;
     }
     dim3 grid((a.D + S::DPB - 1) / S::DPB, a.Bt, sp.S);
-    fwd_kernel<G, VEC, PROJ><<<grid, FWD_THREADS, S::SMEM, stream>>>(
-        a.x, a.dt, a.aneg, a.B, a.C, a.y, a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps, a.proj);
+    fwd_kernel<G, VEC, PROJ, E><<<grid, FWD_THREADS, S::SMEM, stream>>>(
+        reinterpret_cast<const E *>(a.x), reinterpret_cast<const E *>(a.dt), a.aneg, a.B, a.C,
+        reinterpret_cast<E *>(a.y), a.ckpt, a.T, a.D, a.N, a.K, L, sp.cps, a.proj);
     return cudaGetLastError();
 }
 
@@ -577,20 +583,31 @@ static cudaError_t launch_fwd_g(const FwdArgs &a, cudaStream_t stream)
                                   : launch_fwd_gv<G, false>(a, stream);
 }
 
-// bf16 channel arrays: always the whole-state kernel with TMA staging and
-// bulk y stores (the C ABI admits only shapes it covers: 8 < N <= 16,
-// K >= 8, D % 8 == 0, 16-byte aligned x, dt, y).
+// bf16 channel arrays (D % 8 == 0, 16-byte aligned x, dt, y): for 8 < N <= 16
+// and K >= 8 the whole-state kernel with TMA staging and bulk y stores, else
+// the G-lane kernel with 16-byte cp.async staging.
 static cudaError_t launch_fwd_bf16(const FwdArgs &a, cudaStream_t stream)
 {
-    FwdMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    if (groups_for(a.N) != 4 || a.K < 8 || a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt) ||
-        !vec_ok(a.D, a.y, a.y) || !fwd_maps(a, &maps))
+    using BF = __nv_bfloat16;
+    if (a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt) || !vec_ok(a.D, a.y, a.y))
         return cudaErrorInvalidValue;
-    const SegPlan sp = seg_plan_s16(a.Bt, a.T, a.D, a.K);
-    const cudaError_t e = fwd_s16_segments(a, sp, stream);
-    if (e != cudaSuccess) return e;
-    return launch_fwd_s16_p<true, true, true, false, __nv_bfloat16>(a, maps, sp, stream);
+    if (groups_for(a.N) == 4 && a.K >= 8) {
+        FwdMaps maps;
+        memset(&maps, 0, sizeof(maps));
+        if (!fwd_maps(a, &maps)) return cudaErrorInvalidValue;
+        const SegPlan sp = seg_plan_s16(a.Bt, a.T, a.D, a.K);
+        const cudaError_t e = fwd_s16_segments(a, sp, stream);
+        if (e != cudaSuccess) return e;
+        return launch_fwd_s16_p<true, true, true, false, BF>(a, maps, sp, stream);
+    }
+    switch (groups_for(a.N)) {
+    case 1: return launch_fwd_gvp<1, true, false, BF>(a, stream);
+    case 2: return launch_fwd_gvp<2, true, false, BF>(a, stream);
+    case 4: return launch_fwd_gvp<4, true, false, BF>(a, stream);
+    case 8: return launch_fwd_gvp<8, true, false, BF>(a, stream);
+    case 16: return launch_fwd_gvp<16, true, false, BF>(a, stream);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)

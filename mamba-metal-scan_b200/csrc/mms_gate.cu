@@ -23,13 +23,22 @@ namespace mms {
 namespace {
 
 constexpr int GATE_THREADS = 256;
-constexpr int GATE_ROWS = 64;          // rows (b, t) per backward block, at least
+constexpr int GATE_ROWS = 8;           // rows (b, t) per backward block, at least
+constexpr int GATE_BWD_WAVE = 5;       // backward blocks resident per SM (48 registers a thread)
 
-// rows per backward block: GATE_ROWS, or more so that blocks fit grid.y
-long long rows_per_block(long long rows)
+// Rows per backward block: as few as fill one wave of GATE_BWD_WAVE blocks
+// per SM across the grid's channel blocks (a thread keeps 3 arrays x 4 rows
+// of loads in flight, enough to stream HBM at that occupancy), at least
+// GATE_ROWS, and enough that the blocks fit grid.y.
+long long rows_per_block(long long rows, int D)
 {
-    const long long r = (rows + 65534) / 65535;
-    return r > GATE_ROWS ? r : GATE_ROWS;
+    const long long gx = ((D + 3) / 4 + GATE_THREADS - 1) / GATE_THREADS;
+    long long by = (long long)N_SM * GATE_BWD_WAVE / gx;
+    if (by < 1) by = 1;
+    long long r = (rows + by - 1) / by;
+    if (r < GATE_ROWS) r = GATE_ROWS;
+    const long long lim = (rows + 65534) / 65535;
+    return r > lim ? r : lim;
 }
 
 __device__ __forceinline__ float silu_of(float z, float &sig) {
@@ -146,7 +155,7 @@ int grid_for(long long work)
 
 size_t gate_workspace_bytes(long long rows, int D)
 {
-    const long long rpb = rows_per_block(rows);
+    const long long rpb = rows_per_block(rows, D);
     const long long nblk = (rows + rpb - 1) / rpb;
     return (size_t)nblk * D * sizeof(float);
 }
@@ -170,7 +179,7 @@ cudaError_t launch_gate_bwd(const float *dout, const float *y, const float *z, l
 {
     float *part = static_cast<float *>(workspace);
     const int nq = (D + 3) / 4;
-    const long long rpb = rows_per_block(rows);
+    const long long rpb = rows_per_block(rows, D);
     const long long nblk = (rows + rpb - 1) / rpb;
     dim3 grid((nq + GATE_THREADS - 1) / GATE_THREADS, (unsigned)nblk);
     if (vec_ok(D, dout, y, z) && vec_ok(D, dy, dz, dskip) && ldz % 4 == 0)

@@ -214,14 +214,26 @@ static cudaError_t launch_local_g(const SegLocalArgs &a, bool backward, cudaStre
     return v ? launch_local_gv<G, false, true>(a, stream) : launch_local_gv<G, false, false>(a, stream);
 }
 
+template <int G>
+static cudaError_t launch_local_bf16(const SegLocalArgs &a, bool backward, cudaStream_t stream)
+{
+    return backward ? launch_local_gvp<G, true, true, false, __nv_bfloat16>(a, stream)
+                    : launch_local_gvp<G, false, true, false, __nv_bfloat16>(a, stream);
+}
+
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream)
 {
     if (a.bf16) {
-        // bf16 u, dt: the 9..16-state shapes of the bf16 entry points, 16-byte staging
-        if (groups_for(a.N) != 4 || !vec_ok(a.D, a.u, a.dt) || a.D % 8 != 0 || a.proj.on)
-            return cudaErrorInvalidValue;
-        return backward ? launch_local_gvp<4, true, true, false, __nv_bfloat16>(a, stream)
-                        : launch_local_gvp<4, false, true, false, __nv_bfloat16>(a, stream);
+        // bf16 u, dt: 16-byte staging (D % 8 == 0, aligned), no prologue
+        if (!vec_ok(a.D, a.u, a.dt) || a.D % 8 != 0 || a.proj.on) return cudaErrorInvalidValue;
+        switch (groups_for(a.N)) {
+        case 1: return launch_local_bf16<1>(a, backward, stream);
+        case 2: return launch_local_bf16<2>(a, backward, stream);
+        case 4: return launch_local_bf16<4>(a, backward, stream);
+        case 8: return launch_local_bf16<8>(a, backward, stream);
+        case 16: return launch_local_bf16<16>(a, backward, stream);
+        default: return cudaErrorInvalidValue;
+        }
     }
     switch (groups_for(a.N)) {
     case 1: return launch_local_g<1>(a, backward, stream);

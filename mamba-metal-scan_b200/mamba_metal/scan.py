@@ -279,9 +279,6 @@ def selective_scan_proj(x: torch.Tensor, dt_logit: torch.Tensor, a_param: torch.
 
 # ---------------------------------------------------- bf16 storage (f4)
 
-BF16_STATES = (12, 16)
-
-
 def _validate_bf16(x, dt, aneg, b_in, c_in, chunk: int):
     tensors = (x, dt, aneg, b_in, c_in)
     if not all(t.is_cuda for t in tensors) or len({t.device for t in tensors}) != 1:
@@ -299,8 +296,8 @@ def _validate_bf16(x, dt, aneg, b_in, c_in, chunk: int):
     if aneg.shape[0] != d or b_in.shape != (bt, t_len, n) or c_in.shape != (bt, t_len, n):
         raise ValueError(f"Aneg {tuple(aneg.shape)}, B {tuple(b_in.shape)}, C {tuple(c_in.shape)} "
                          f"do not match x {tuple(x.shape)}")
-    if n not in BF16_STATES:
-        raise ValueError(f"the bf16 scan supports d_state {BF16_STATES}; got {n}")
+    if n % 4 != 0 or n <= 0 or n > 64:
+        raise ValueError(f"d_state must be a positive multiple of 4 no larger than 64; got {n}")
     if d % 8 != 0:
         raise ValueError(f"the bf16 scan needs d_inner % 8 == 0; got {d}")
     if chunk != 8:
@@ -362,9 +359,9 @@ def selective_scan_bf16(x: torch.Tensor, dt: torch.Tensor, aneg: torch.Tensor,
 
     Same recurrence and autograd contract as `selective_scan`; x and dt are
     bf16 CUDA tensors, Aneg, B and C any float dtype (used as fp32), y is
-    bf16. Covers d_state 12 or 16, d_inner a multiple of 8, chunk 8 (the
-    shapes of the whole-state forward and the 8-state backward kernels);
-    other shapes raise ValueError.
+    bf16. Covers every d_state of the fp32 scan with d_inner a multiple of 8
+    and checkpoint stride 8 (bf16 rows are staged in 16-byte pieces; the
+    backward uses the stride-8 kernels); other shapes raise ValueError.
     """
     return SelectiveScanBF16CUDA.apply(x, dt, aneg, b_in, c_in, chunk, return_state)
 

@@ -9,7 +9,8 @@ test pins bf16 results. Two checks stand in:
   tolerance BF16_TOL = 2^-8); dAneg, dB and dC are fp32 outputs of fp32
   arithmetic on those values and keep the fp32 scan's 1e-4;
 * against the fp32 entry points on the widened inputs, where both run the
-  same kernel (the whole-state forward, the 8-state backward): every fp32
+  same kernels (whole-state or G-lane forward, 8- or 4-state backward, time
+  segments): every fp32
   output is bit-identical and every bf16 output equals the fp32 one rounded
   to nearest even. So the storage type changes the loads and the final
   rounding and nothing else.
@@ -32,16 +33,24 @@ GRAD_TOL = 1e-4
 
 # (Bt, T, D, N): whole-state forward with and without time segments, T not a
 # multiple of the 8-step chunk or the 16-step tile, D not a multiple of the
-# 128-channel CTA, d_state 12.
+# 128-channel CTA, d_state 12; the G-lane forward and 4-state backward at
+# every other lane count (d_state 4, 8, 20, 32, 64), with time segments.
 CASES = [
     (16, 64, 2304, 16),
     (2, 77, 40, 16),
     (3, 50, 24, 12),
     (1, 3000, 64, 16),
     (1, 9, 8, 16),
+    (2, 33, 24, 4),
+    (2, 77, 40, 8),
+    (3, 40, 32, 20),
+    (2, 100, 64, 32),
+    (1, 50, 16, 64),
+    (1, 2000, 32, 32),
 ]
 # shapes where the fp32 entry points run the same kernels as the bf16 ones
-SAME_PATH = [(16, 64, 2304, 16), (12, 40, 2048, 12), (1, 3000, 64, 16)]
+SAME_PATH = [(16, 64, 2304, 16), (12, 40, 2048, 12), (1, 3000, 64, 16), (2, 100, 64, 32),
+             (1, 64, 40, 8), (1, 2000, 32, 32)]
 
 
 def _bf16_inputs(bt, t_len, d, n, seed):
@@ -109,7 +118,7 @@ def test_bf16_gradients_follow_the_input_dtypes():
 
 
 def test_bf16_shape_rules_raise_before_any_launch():
-    xb, dtb, aneg, b_in, c_in, _ = _bf16_inputs(1, 16, 16, 8, SEED)
+    xb, dtb, aneg, b_in, c_in, _ = _bf16_inputs(1, 16, 16, 6, SEED)
     args = [t.to(DEV) for t in (xb, dtb, aneg, b_in, c_in)]
     with pytest.raises(ValueError, match="d_state"):
         selective_scan_bf16(*args)
@@ -126,4 +135,4 @@ def test_bf16_shape_rules_raise_before_any_launch():
     # the C ABI answers the same shapes with its own status, before launching
     lib = _native.load()
     p = [t.data_ptr() for t in args] + [args[0].data_ptr(), args[2].data_ptr()]
-    assert lib.mms_fwd_bf16(*p, 1, 16, 16, 16, 4, None) == _native.MMS_ERR_UNSUPPORTED_BF16
+    assert lib.mms_fwd_bf16(*p, 1, 16, 12, 16, 8, None) == _native.MMS_ERR_UNSUPPORTED_BF16

@@ -67,16 +67,16 @@ def test_bad_arguments_return_status_without_launching():
 
 
 def test_bf16_entry_points_check_their_shapes_first():
-    """bf16 storage covers 8 < N <= 16, D % 8 == 0, K == 8 (forward K >= 8)."""
+    """bf16 storage needs D % 8 == 0, and K == 8 for the backward (fake pointers:
+    every call here must be refused before a launch)."""
     lib = _native.load()
     null = None
     fake = [ctypes.c_void_p(0x10000)] * 7
     unsup = _native.MMS_ERR_UNSUPPORTED_BF16
-    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 8, 8, null) == unsup       # N = 8
-    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 20, 8, null) == unsup      # N = 20
     assert lib.mms_fwd_bf16(*fake, 2, 8, 12, 16, 8, null) == unsup      # D % 8
-    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 16, 4, null) == unsup      # K < 8
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 20, 32, 1, null) == unsup      # D % 8
     assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 6, 8, null) == _native.MMS_ERR_UNSUPPORTED_N
+    assert lib.mms_fwd_bf16(*fake, 2, 8, 16, 68, 8, null) == _native.MMS_ERR_UNSUPPORTED_N
     assert lib.mms_fwd_bf16(*([null] * 7), 2, 8, 16, 16, 8, null) == _native.MMS_ERR_INVALID_ARG
     # bf16 arrays need 16-byte alignment (fp32 ones: 16 as before)
     odd = [ctypes.c_void_p(0x10008)] + [ctypes.c_void_p(0x10000)] * 6
@@ -85,6 +85,8 @@ def test_bf16_entry_points_check_their_shapes_first():
     need = lib.mms_bwd_workspace_size(2, 8, 16, 16, 8)
     ws = ctypes.c_void_p(0x20000)
     assert lib.mms_bwd_bf16(*bargs, ws, need, 2, 8, 16, 16, 16, null) == unsup   # K != 8
+    assert lib.mms_bwd_bf16(*bargs, ws, need, 2, 8, 16, 64, 4, null) == unsup    # K != 8
+    assert lib.mms_bwd_bf16(*bargs, ws, need, 2, 8, 20, 16, 8, null) == unsup    # D % 8
     assert lib.mms_bwd_bf16(*bargs, ws, need - 1, 2, 8, 16, 16, 8, null) == _native.MMS_ERR_WORKSPACE
 
 
