@@ -404,6 +404,9 @@ def run_native(args, shape):
     if kk == 8 and n in (12, 16) and d % 8 == 0 and world == 1 and not args.no_bf16:
         line["bf16"] = time_bf16(lib, _native, shape, device, (x, dt, aneg, b_in, c_in, dy),
                                  stream, hbm_gbs)
+        if not args.no_e2e:
+            line["bf16"]["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan,
+                                          bf16=True)
     # e2e through the public API from pinned host buffers
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan, channel)
@@ -507,10 +510,16 @@ def time_bf16(lib, _native, shape, device, ins, stream, hbm_gbs, k=20):
             "note": "bf16 x, dt, y, dy, dx, ddt; fp32 arithmetic, Aneg, B, C, ckpt; kernels only"}
 
 
-def run_e2e(args, shape, device, world, rank, selective_scan, channel=False):
+def run_e2e(args, shape, device, world, rank, selective_scan, channel=False, bf16=False):
+    """bf16: x, dt, dy and y, dx, ddt cross PCIe as bf16 (selective_scan_bf16)."""
     bt, t_len, d_total, n, kk = shape
     host = make_inputs(bt, t_len, d_total, n, 2000 + (0 if channel else rank), "cpu")
-    if channel:
+    cd = torch.bfloat16 if bf16 else torch.float32        # channel arrays' storage
+    if bf16:
+        from mamba_metal import selective_scan_bf16
+        host = [t.to(cd) if t.dim() == 3 and t.shape[2] == d_total else t for t in host]
+        scan = lambda *a: selective_scan_bf16(*a, chunk=kk)  # noqa: E731
+    elif channel:
         from mamba_metal.sharded import channel_shard, selective_scan_channel_sharded
         sl = channel_shard(d_total, world, rank)
         host = [t[:, :, sl] if t.dim() == 3 and t.shape[2] == d_total else t for t in host]
@@ -520,11 +529,11 @@ def run_e2e(args, shape, device, world, rank, selective_scan, channel=False):
         scan = lambda *a: selective_scan(*a, impl="cuda", chunk=kk)  # noqa: E731
     host = [t.contiguous().pin_memory() for t in host]
     d = host[0].shape[2]
-    outs_h = [torch.empty(bt, t_len, d).pin_memory() for _ in range(3)] + \
+    outs_h = [torch.empty(bt, t_len, d, dtype=cd).pin_memory() for _ in range(3)] + \
              [torch.empty(d, n).pin_memory(), torch.empty(bt, t_len, n).pin_memory(),
               torch.empty(bt, t_len, n).pin_memory()]
-    h2d = sum(t.numel() * 4 for t in host)
-    d2h = sum(t.numel() * 4 for t in outs_h)
+    h2d = sum(t.numel() * t.element_size() for t in host)
+    d2h = sum(t.numel() * t.element_size() for t in outs_h)
     # Three streams, as a training or serving loop would run them: copies in
     # (step i+1) and out (step i-1) overlap the scan of step i; the inputs are
     # double-buffered on the device and every step copies all of them in and
@@ -573,9 +582,10 @@ def run_e2e(args, shape, device, world, rank, selective_scan, channel=False):
     torch.cuda.synchronize()
     t_ms = max_over_ranks(s.elapsed_time(e), world, device)
     total = bt * t_len * d_total if channel else world * bt * t_len * d
+    api = ("mamba_metal.selective_scan_bf16" if bf16 else "mamba_metal.selective_scan(impl='cuda')")
     return {"value": total * k / (t_ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": k,
-            "api": "mamba_metal.selective_scan(impl='cuda') + torch.autograd.grad, pinned host I/O; "
+            "api": api + " + torch.autograd.grad, pinned host I/O; "
                    "copies in / out on their own streams, overlapping the previous and next step"}
 
 
