@@ -465,7 +465,7 @@ bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
 
 }  // namespace
 
-bool bwd_w8_applies(int N, int K) { return groups_for(N) == 4 && N > 8 && K == W8_CH; }
+bool bwd_w8_applies(int N, int K) { return K == W8_CH && w8_shape(N, K); }
 
 #ifndef MMS_BWD_TMA
 #define MMS_BWD_TMA 1

@@ -87,6 +87,9 @@ struct SegPlan {
     int cps;    // checkpoint chunks per segment
 };
 
+// The shapes of the 8-state backward (mms_bwd_w8.cu): 8 < N <= 16, K == 8.
+inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8; }
+
 inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
 {
     const int dpb = 256 / groups_for(N);
@@ -96,8 +99,11 @@ inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
     // Splitting costs a local pass over S-1 segments (about 40 % more work for
     // a fwd+bwd step), which pays only below one CTA per SM.
     if (base >= N_SM) return p;
-    // segments for whole waves of the backward (4 CTAs of 64 channels per SM)
-    const long long want = (4LL * N_SM) / base;
+    // Segments for one whole wave of the backward: the 8-state kernel runs 4
+    // CTAs per SM, the 4-state kernels (and the G-lane forward) 2. More
+    // segments than one wave holds only add local-pass work.
+    const long long per_sm = w8_shape(N, K) ? 4 : 2;
+    const long long want = (per_sm * N_SM) / base;
     long long cps = (nchunk + want - 1) / want;
     if (cps < 2) cps = 2;                           // the forward keeps P_s in chunk cps-2
     if (cps * K < 64) cps = (64 + K - 1) / K;       // at least 64 steps per segment
