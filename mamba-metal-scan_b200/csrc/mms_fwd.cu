@@ -193,7 +193,9 @@ struct S16Shape {
     static constexpr size_t CKF = (size_t)2 * 2 * DPB * 16;  // [2][2][DPB*N]
     static constexpr size_t SMEM = sizeof(float) * TILEF;
     static constexpr size_t SMEM_BULK = sizeof(float) * (TILEF + YF + CKF);
-    static constexpr size_t SMEM_TMA = SMEM_BULK + 64;       // + the stage barriers
+    // + 1 KB to align the checkpoint slabs for their swizzled TMA stores,
+    // + the stage barriers
+    static constexpr size_t SMEM_TMA = SMEM_BULK + 1024 + 64;
     static constexpr uint32_t TILE_BYTES = sizeof(float) * S16_TT * ROWF;
 };
 
@@ -207,9 +209,10 @@ struct S16Tile {
 static_assert(S16Tile<float>::BYTES == S16Shape::TILE_BYTES, "fp32 TMA tile is the full tile");
 
 // Tensor maps of the TMA staging path: x, dt (D, T, Bt) with 128 x 16 boxes,
-// B, C (N, T, Bt) with 16 x 16 boxes.
+// B, C (N, T, Bt) with 16 x 16 boxes; ckpt (N, D, nchunk, Bt) with 16 x 128
+// boxes in the 64-byte swizzled shared layout (stores of checkpoint slabs).
 struct FwdMaps {
-    CUtensorMap x, dt, B, C;
+    CUtensorMap x, dt, B, C, ck;
 };
 
 // Set when a wait on a forward TMA stage gave up; read by mms_device_status().
@@ -249,7 +252,14 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     float *tiles = smem;                                   // [STAGES][TT][ROWF]
     float *ys = smem + S16Shape::TILEF;                    // BULK: [2][TT][DPB] of E
     E *yse = reinterpret_cast<E *>(ys);
-    float *cks = ys + S16Shape::YF;                        // BULK: [2][2][DPB*N]
+    // BULK: [2][2] checkpoint slabs. cp.async path: [DPB][N] rows, sent by bulk
+    // copies. TMA path: [DPB][16] rows in the 64-byte swizzled layout (state
+    // quad q of channel c at quad q ^ ((c >> 1) & 3), so a warp's 16-byte
+    // stores of 32 channels hit all banks), 1024-byte aligned, sent by TMA
+    // tile stores that undo the swizzle.
+    float *cks = ys + S16Shape::YF;
+    if constexpr (TMA) cks += ((1024u - (smem_u32(cks) & 1023u)) & 1023u) / 4u;
+    constexpr int CKROW = TMA ? 16 : 0;                    // TMA slab row (floats); else N
     const uint32_t bars = smem_u32(cks + S16Shape::CKF);   // TMA: FWD_STAGES barriers
 
     const int tid = threadIdx.x;
@@ -304,9 +314,14 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
         for (int r = 0; r < rows; ++r)
             bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB,
                        dcnt * (uint32_t)sizeof(E));
-        for (int i = 0; i < nck; ++i)
-            bulk_store(ckpt + ((size_t)b * nchunk + (i ? ck1 : ck0)) * D * N + (size_t)d0 * N,
-                       cks + ((kp & 1) * 2 + i) * DPB * N, (uint32_t)dcnt * N * 4u);
+        for (int i = 0; i < nck; ++i) {
+            if constexpr (TMA)
+                tma_store4(&maps.ck, smem_u32(cks + ((kp & 1) * 2 + i) * DPB * CKROW), 0, d0,
+                           i ? ck1 : ck0, b);
+            else
+                bulk_store(ckpt + ((size_t)b * nchunk + (i ? ck1 : ck0)) * D * N + (size_t)d0 * N,
+                           cks + ((kp & 1) * 2 + i) * DPB * N, (uint32_t)dcnt * N * 4u);
+        }
         bulk_commit();
     };
 
@@ -403,8 +418,14 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
             if (t == next_ck && (!SEG || t < te)) {        // uniform across the CTA
                 float *o = ckb + (size_t)chunk * D * N;
                 const bool keep = SEG && chunk == ck_keep;
+                int swz = 0;                               // quad index XOR (TMA slabs)
                 if (BULK && nck < 2 && !keep) {
-                    o = cks + ((k & 1) * 2 + nck) * DPB * N + tid * N;
+                    if constexpr (TMA) {
+                        o = cks + ((k & 1) * 2 + nck) * DPB * CKROW + tid * CKROW;
+                        swz = (tid >> 1) & 3;
+                    } else {
+                        o = cks + ((k & 1) * 2 + nck) * DPB * N + tid * N;
+                    }
                     if (nck == 0) ck0 = chunk; else ck1 = chunk;
                     ++nck;
                 }
@@ -412,8 +433,8 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
 #pragma unroll
                     for (int q = 0; q < 4; ++q)
                         if (4 * q < N)
-                            st4(o + 4 * q, make_float4(h[2 * q].x, h[2 * q].y, h[2 * q + 1].x,
-                                                       h[2 * q + 1].y));
+                            st4(o + 4 * (q ^ swz), make_float4(h[2 * q].x, h[2 * q].y,
+                                                               h[2 * q + 1].x, h[2 * q + 1].y));
                 }
                 ++chunk;
                 next_ck = min(next_ck + K, T - 1);
@@ -514,7 +535,11 @@ static bool fwd_maps(const FwdArgs &a, FwdMaps *m)
     const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
     const cuuint32_t bB[3] = {16, S16_TT, 1};
     const int ex = a.bf16 ? 2 : 4;
-    return tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
+    const int nchunk = (a.T + a.K - 1) / a.K;
+    const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
+    const cuuint32_t bK[4] = {16, S16_DPB, 1, 1};
+    return tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK, 4, CU_TENSOR_MAP_SWIZZLE_64B) &&
+           tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
            tma_encode(fn, &m->B, a.B, 3, dB, bB) && tma_encode(fn, &m->C, a.C, 3, dB, bB);
 }
 

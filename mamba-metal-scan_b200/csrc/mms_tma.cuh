@@ -46,6 +46,16 @@ __device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap *m, int c0,
                  : "memory");
 }
 
+// TMA tile store of a 4-D box from this CTA's shared memory to global memory,
+// tracked by the bulk-group commit / wait of bulk_store. Every coordinate is
+// non-negative; elements of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store4(const CUtensorMap *m, uint32_t src, int c0, int c1,
+                                           int c2, int c3) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group"
+                 " [%0, {%1, %2, %3, %4}], [%5];\n"
+                 ::"l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(src)
+                 : "memory");
+}
 
 inline PFN_cuTensorMapEncodeTiled_v12000 tma_encoder()
 {
@@ -64,9 +74,12 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tma_encoder()
 
 // Tile map over a row-major array of fp32 (elem 4) or bf16 (elem 2) whose
 // innermost `rank` dims are `dim` (dim[0] contiguous), box `box`;
-// out-of-range elements load as zeros.
+// out-of-range elements load as zeros. `swz` is the shared-memory layout of a
+// box (CU_TENSOR_MAP_SWIZZLE_64B: the 16-byte piece j of 64-byte row r sits
+// at piece j ^ ((r >> 1) & 3), on a 1024-byte aligned box).
 inline bool tma_encode(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap *m, const void *base, int rank,
-            const cuuint64_t *dim, const cuuint32_t *box, int elem = 4)
+            const cuuint64_t *dim, const cuuint32_t *box, int elem = 4,
+            CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_NONE)
 {
     cuuint64_t stride[4];
     cuuint64_t s = (cuuint64_t)elem;
@@ -77,7 +90,7 @@ inline bool tma_encode(PFN_cuTensorMapEncodeTiled_v12000 fn, CUtensorMap *m, con
     const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     const CUtensorMapDataType ty = elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     return fn(m, ty, rank, const_cast<void *>(base), dim, stride, box,
-              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
               CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
