@@ -28,6 +28,20 @@ namespace mms {
 constexpr int FWD_THREADS = 256;
 constexpr int FWD_STAGES = 3;
 
+// Where lane g's y partial of row p (= step * DPB + channel) sits in the
+// [TT*DPB][G] partial buffer. For G >= 8 a row spans 2 or 4 float4 quads;
+// quad (g >> 2) is stored at quad (g >> 2) ^ f(p), so the reduction's float4
+// reads of consecutive rows touch every bank group (rows at 32- or 64-byte
+// stride would otherwise put 8 or 16 lanes on the same banks). The reduction
+// reads the quads in logical order, so sums are unchanged.
+template <int G>
+__device__ __forceinline__ int ys_at(int p, int g)
+{
+    if constexpr (G == 16) return p * 16 + 4 * ((g >> 2) ^ ((p >> 1) & 3)) + (g & 3);
+    else if constexpr (G == 8) return p * 8 + 4 * ((g >> 2) ^ ((p >> 2) & 1)) + (g & 3);
+    else return p * G + g;
+}
+
 template <int G>
 struct FwdShape {
     static constexpr int DPB = FWD_THREADS / G;            // channels per CTA
@@ -134,7 +148,7 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
             h[0] = fma2(ex2x2(mul2(dt2, nan2[0])), h[0], mul2(bx2, lo(Bv)));
             h[1] = fma2(ex2x2(mul2(dt2, nan2[1])), h[1], mul2(bx2, hi(Bv)));
             const float2 acc = fma2(hi(Cv), h[1], mul2(lo(Cv), h[0]));
-            ys[(j * DPB + c) * G + g] = acc.x + acc.y;
+            ys[ys_at<G>(j * DPB + c, g)] = acc.x + acc.y;
             if (t0 + j == next_ck && t0 + j < te) {        // uniform across the CTA
                 if (act && chunk != ck_keep)
                     st4(ckb + (size_t)chunk * D * N, make_float4(h[0].x, h[0].y, h[1].x, h[1].y));
@@ -146,15 +160,15 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
         // y = sum of the G lane partials; consecutive threads take consecutive channels.
         for (int p = tid; p < TT * DPB; p += FWD_THREADS) {
             const int j = p / DPB, cc = p % DPB;
-            const float *src = ys + (size_t)p * G;
             float sum = 0.f;
             if constexpr (G >= 4) {
 #pragma unroll
                 for (int q = 0; q < G; q += 4) {
-                    const float4 v = *reinterpret_cast<const float4 *>(src + q);
+                    const float4 v = *reinterpret_cast<const float4 *>(ys + ys_at<G>(p, q));
                     sum += (v.x + v.y) + (v.z + v.w);
                 }
             } else {
+                const float *src = ys + (size_t)p * G;
 #pragma unroll
                 for (int q = 0; q < G; ++q) sum += src[q];
             }
@@ -177,7 +191,8 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
 // Per tile of 16 steps: y rows [16][128] and up to two checkpoint slabs of
 // 128 channels x N (each a contiguous block of ckpt), double buffered; a
 // third checkpoint in one tile (only the t = T-1 one can be) is stored
-// directly.
+// directly. With TMA staging the slabs are sent by TMA tile stores from a
+// swizzled layout (see fwd_kernel_s16), otherwise by plain bulk copies.
 #ifndef MMS_FWD_ACC
 #define MMS_FWD_ACC 4
 #endif
