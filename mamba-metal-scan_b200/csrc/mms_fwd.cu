@@ -224,10 +224,11 @@ struct S16Tile {
 static_assert(S16Tile<float>::BYTES == S16Shape::TILE_BYTES, "fp32 TMA tile is the full tile");
 
 // Tensor maps of the TMA staging path: x, dt (D, T, Bt) with 128 x 16 boxes,
-// B, C (N, T, Bt) with 16 x 16 boxes; ckpt (N, D, nchunk, Bt) with 16 x 128
-// boxes in the 64-byte swizzled shared layout (stores of checkpoint slabs).
+// B, C (N, T, Bt) with 16 x 16 boxes; for the stores, y (D, T, Bt) with
+// 128 x 16 boxes and ckpt (N, D, nchunk, Bt) with 16 x 128 boxes in the
+// 64-byte swizzled shared layout.
 struct FwdMaps {
-    CUtensorMap x, dt, B, C, ck;
+    CUtensorMap x, dt, B, C, y, ck;
 };
 
 // Set when a wait on a forward TMA stage gave up; read by mms_device_status().
@@ -326,9 +327,15 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     auto send = [&](int kp, int nck, int ck0, int ck1) {
         const int t0p = tb + kp * TT, rows = min(TT, te - t0p);
         const E *ysrc = yse + (kp & 1) * TT * DPB;
-        for (int r = 0; r < rows; ++r)
-            bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB,
-                       dcnt * (uint32_t)sizeof(E));
+        if (TMA && (!SEG || rows == TT)) {
+            // one tile store; rows past T and channels past D are not written
+            tma_store3(&maps.y, smem_u32(ysrc), d0, t0p, b);
+        } else {
+            // a segment's last rows stop at te, inside the tensor: row by row
+            for (int r = 0; r < rows; ++r)
+                bulk_store(y + ((size_t)b * T + t0p + r) * D + d0, ysrc + r * DPB,
+                           dcnt * (uint32_t)sizeof(E));
+        }
         for (int i = 0; i < nck; ++i) {
             if constexpr (TMA)
                 tma_store4(&maps.ck, smem_u32(cks + ((kp & 1) * 2 + i) * DPB * CKROW), 0, d0,
@@ -554,6 +561,7 @@ static bool fwd_maps(const FwdArgs &a, FwdMaps *m)
     const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
     const cuuint32_t bK[4] = {16, S16_DPB, 1, 1};
     return tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK, 4, CU_TENSOR_MAP_SWIZZLE_64B) &&
+           tma_encode(fn, &m->y, a.y, 3, dX, bX, ex) &&
            tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
            tma_encode(fn, &m->B, a.B, 3, dB, bB) && tma_encode(fn, &m->C, a.C, 3, dB, bB);
 }

@@ -49,6 +49,13 @@ __device__ __forceinline__ void tma4(uint32_t dst, const CUtensorMap *m, int c0,
 // TMA tile store of a 4-D box from this CTA's shared memory to global memory,
 // tracked by the bulk-group commit / wait of bulk_store. Every coordinate is
 // non-negative; elements of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store3(const CUtensorMap *m, uint32_t src, int c0, int c1,
+                                           int c2) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group"
+                 " [%0, {%1, %2, %3}], [%4];\n"
+                 ::"l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2), "r"(src)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_store4(const CUtensorMap *m, uint32_t src, int c0, int c1,
                                            int c2, int c3) {
     asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group"
