@@ -197,7 +197,13 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
 #define MMS_FWD_ACC 4
 #endif
 constexpr int S16_DPB = 128;                                 // channels (= threads) per CTA
-constexpr int S16_TT = 16;
+#ifndef MMS_S16_TT
+#define MMS_S16_TT 16
+#endif
+#ifndef MMS_S16_MINB
+#define MMS_S16_MINB 2
+#endif
+constexpr int S16_TT = MMS_S16_TT;                           // steps per staged tile
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
 struct S16Shape {
@@ -246,7 +252,7 @@ __device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
 // like the cp.async path's zero fill.
 // E: storage type of x, dt and y (float, or bf16 with TMA staging only).
 template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG, typename E>
-__global__ void __launch_bounds__(S16_DPB, 2)
+__global__ void __launch_bounds__(S16_DPB, MMS_S16_MINB)
 fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, E *__restrict__ y,
@@ -485,7 +491,7 @@ static SegPlan seg_plan_s16(int Bt, int T, int D, int K)
     const int nchunk = (T + K - 1) / K;
     SegPlan p{1, nchunk};
     if (base >= N_SM) return p;
-    const long long want = (2LL * N_SM) / base;
+    const long long want = ((long long)MMS_S16_MINB * N_SM) / base;
     long long cps = (nchunk + want - 1) / want;
     if (cps < 2) cps = 2;                           // P_s is kept in chunk cps-2
     if (cps * K < 64) cps = (64 + K - 1) / K;
