@@ -203,6 +203,10 @@ constexpr int S16_DPB = 128;                                 // channels (= thre
 #ifndef MMS_S16_MINB
 #define MMS_S16_MINB 2
 #endif
+#ifndef MMS_S16_UNROLL
+#define MMS_S16_UNROLL 4
+#endif
+constexpr int S16_UNROLL = MMS_S16_UNROLL;                   // steps unrolled in the tile loop
 constexpr int S16_TT = MMS_S16_TT;                           // steps per staged tile
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
@@ -416,7 +420,7 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
         E *yrow = yse + (k & 1) * TT * DPB + tid;
         const int t0 = tb + k * TT;
         nck = 0;
-#pragma unroll 4
+#pragma unroll S16_UNROLL
         for (int j = 0; j < TT; ++j) {
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
             const float xv = to_f(tx[j * XROW + tid]);
