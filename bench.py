@@ -72,7 +72,7 @@ def _splits(bt, t_len, d, n, k, dpb, ctas_per_sm):
 
 
 def launches_per_step(bt, t_len, d, n, k):
-    """Kernels of one mms_fwd + mms_bwd: 1 + 3, plus a local pass and a
+    """Kernels of one mms_fwd + mms_bwd: 1 + 2, plus a local pass and a
     combine in each direction that cuts time into segments."""
     g = 1
     while g < (n + 3) // 4:
@@ -85,7 +85,7 @@ def launches_per_step(bt, t_len, d, n, k):
         split_f = True                                    # whole-state forward, segmented
     else:
         split_f = _splits(bt, t_len, d, n, k, 256 // g, per_sm)
-    return 4 + 2 * split_f + 2 * split_b
+    return 3 + 2 * split_f + 2 * split_b
 
 
 def make_inputs(bt, t_len, d, n, seed, device):
@@ -382,7 +382,7 @@ def run_native(args, shape):
                                    f"batch-shard x{world} (no collective)"),
                    "l2": "inputs larger than L2 (%.0f MB touched per step)" % ((fwd_b + bwd_b) / 1e6)},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-        "roofline": {"kernel": "mms_bwd (bwd_kernel_w8 + 2 reduce kernels)", "bound": "hbm",
+        "roofline": {"kernel": "mms_bwd (bwd_kernel_w8 + reduce_kernel)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                      "frac": achieved / hbm_gbs, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",

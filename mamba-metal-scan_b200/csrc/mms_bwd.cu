@@ -43,9 +43,9 @@
 //     butterfly levels every lane keeps registers {0,1} and then {0}, so only
 //     the last level (dB vs dC) needs selects. The CTA's warps are summed in
 //     shared memory once per group into one partial per CTA, and
-//     reduce_bc_kernel adds the CTAs of a batch row;
+//     reduce_kernel adds the CTAs of a batch row;
 //   * dAneg: per-thread register sums over the whole walk, one partial per
-//     batch row; reduce_a_kernel adds the rows.
+//     batch row; reduce_kernel adds the rows.
 #include "mms_common.cuh"
 #include "mms_kernels.h"
 #include "mms_stage.cuh"
@@ -704,36 +704,59 @@ bwd_kernel_k8(const E *__restrict__ x, const E *__restrict__ dt,
     store_dacc<G>(L, A, part_a, D, N);
 }
 
-// dB|dC = sum over the nblk CTA partials of each batch row (fixed order).
-__global__ void reduce_bc_kernel(const float *__restrict__ part, float *__restrict__ dB,
-                                 float *__restrict__ dC, int Bt, int T, int N, int nblk)
+// The backward's two fixed-order reductions in one launch. Blocks
+// [0, nb_bc): dB|dC = sum over the nblk CTA partials of each batch row.
+// The other blocks: dAneg = sum over the (batch row, time segment) partials;
+// with the prologue, the gradient of the raw A is dAneg * softplus'(A) =
+// dAneg * sigmoid(A). A thread takes 4 consecutive outputs (float4): with
+// N % 4 == 0 no quad straddles dB and dC and every quad is 16-byte aligned.
+// Each output is summed in the same order as one scalar loop would.
+__global__ void reduce_kernel(const float *__restrict__ part_bc, float *__restrict__ dB,
+                              float *__restrict__ dC, int Bt, int T, int N, int nblk, int nb_bc,
+                              const float *__restrict__ part_a, float *__restrict__ daneg,
+                              int rows, size_t DN, const float *__restrict__ a_raw, int proj)
 {
-    const size_t per_b = (size_t)T * 2 * N;
-    const size_t total = (size_t)Bt * per_b;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        const size_t b = idx / per_b, r = idx - b * per_b;
-        const float *p = part + b * nblk * per_b + r;
-        float s = 0.f;
-        for (int k = 0; k < nblk; ++k) s += p[(size_t)k * per_b];
-        const size_t t = r / (2 * N);
-        const int j = (int)(r - t * 2 * N);
-        if (j < N) dB[(b * T + t) * N + j] = s;
-        else dC[(b * T + t) * N + (j - N)] = s;
+    if ((int)blockIdx.x < nb_bc) {
+        const size_t per_b = (size_t)T * 2 * N;
+        const size_t quads = (size_t)Bt * per_b / 4;
+        for (size_t qi = (size_t)blockIdx.x * blockDim.x + threadIdx.x; qi < quads;
+             qi += (size_t)nb_bc * blockDim.x) {
+            const size_t idx = 4 * qi;
+            const size_t b = idx / per_b, r = idx - b * per_b;
+            const float *p = part_bc + b * nblk * per_b + r;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < nblk; ++k) {
+                const float4 v = ld4(p + (size_t)k * per_b);
+                sum.x += v.x;
+                sum.y += v.y;
+                sum.z += v.z;
+                sum.w += v.w;
+            }
+            const size_t t = r / (2 * N);
+            const int j = (int)(r - t * 2 * N);
+            st4(j < N ? dB + (b * T + t) * N + j : dC + (b * T + t) * N + (j - N), sum);
+        }
+        return;
     }
-}
-
-// dAneg = sum over the (batch row, time segment) partials (fixed order).
-// With the prologue, the gradient of the raw A is dAneg * softplus'(A) = dAneg * sigmoid(A).
-__global__ void reduce_a_kernel(const float *__restrict__ part, float *__restrict__ daneg,
-                                int rows, size_t DN, const float *__restrict__ a_raw, int proj)
-{
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < DN;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        float s = 0.f;
-        for (int r = 0; r < rows; ++r) s += part[(size_t)r * DN + idx];
-        if (proj) s *= 1.f / (1.f + expf(-a_raw[idx]));
-        daneg[idx] = s;
+    const size_t nb_a = gridDim.x - nb_bc;
+    for (size_t qi = (size_t)(blockIdx.x - nb_bc) * blockDim.x + threadIdx.x; qi < DN / 4;
+         qi += nb_a * blockDim.x) {
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < rows; ++r) {
+            const float4 v = ld4(part_a + (size_t)r * DN + 4 * qi);
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
+        }
+        if (proj) {
+            const float4 a = ld4(a_raw + 4 * qi);
+            sum.x *= 1.f / (1.f + expf(-a.x));
+            sum.y *= 1.f / (1.f + expf(-a.y));
+            sum.z *= 1.f / (1.f + expf(-a.z));
+            sum.w *= 1.f / (1.f + expf(-a.w));
+        }
+        st4(daneg + 4 * qi, sum);
     }
 }
 
@@ -808,13 +831,16 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps, a.proj);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    const size_t nbc = (size_t)a.Bt * a.T * 2 * a.N;
-    const int rb = (int)((nbc + 255) / 256 < 148 * 16 ? (nbc + 255) / 256 : 148 * 16);
-    reduce_bc_kernel<<<rb, 256, 0, stream>>>(part_bc, a.dB, a.dC, a.Bt, a.T, a.N, w.nblk);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    auto blocks = [](size_t quads) {
+        const size_t b = (quads + 255) / 256;
+        return (int)(b < (size_t)N_SM * 16 ? b : (size_t)N_SM * 16);
+    };
+    const int nb_bc = blocks((size_t)a.Bt * a.T * 2 * a.N / 4);
     const size_t dn = (size_t)a.D * a.N;
-    const int ra = (int)((dn + 255) / 256 < 148 * 16 ? (dn + 255) / 256 : 148 * 16);
-    reduce_a_kernel<<<ra, 256, 0, stream>>>(part_a, a.daneg, a.Bt * sp.S, dn, a.aneg, a.proj.on);
+    const int nb_a = blocks(dn / 4);
+    reduce_kernel<<<nb_bc + nb_a, 256, 0, stream>>>(part_bc, a.dB, a.dC, a.Bt, a.T, a.N, w.nblk,
+                                                    nb_bc, part_a, a.daneg, a.Bt * sp.S, dn,
+                                                    a.aneg, a.proj.on);
     return cudaGetLastError();
 }
 

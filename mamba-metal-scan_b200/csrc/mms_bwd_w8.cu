@@ -26,7 +26,7 @@
 //     bits 4, 3, 2 (where the lane's state order r XOR tau, tau = lane bits
 //     2..4, makes every level select-free) and a last transposed level over
 //     lane bit 1 (dB vs dC). Each lane ends with one value; the CTA's four
-//     warps are summed per step into one partial per CTA (reduce_bc_kernel
+//     warps are summed per step into one partial per CTA (reduce_kernel
 //     adds the CTAs);
 //   * dAneg: register sums over the walk, one partial per (batch row, time
 //     segment).
