@@ -786,7 +786,7 @@ def main():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     ap.add_argument("--chunk", type=int, default=None, help="checkpoint stride (default: the config's, 8)")
-    ap.add_argument("--cpu-budget", type=float, default=10.0,
+    ap.add_argument("--cpu-budget", type=float, default=18.0,
                     help="seconds of CPU work for the cpu_baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
