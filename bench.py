@@ -79,12 +79,13 @@ def launches_per_step(bt, t_len, d, n, k):
         g *= 2
     per_sm = 4 if (8 < n <= 16 and k == 8) else 2         # backward CTAs per SM
     split_b = _splits(bt, t_len, d, n, k, 256 // g, per_sm)
+    split_g = _splits(bt, t_len, d, n, k, 256 // g, per_sm)  # the G-lane forward's plan
     if 8 < n <= 16 and bt * d >= N_SM * 128:
         split_f = False                                   # whole-state forward, no split
-    elif 8 < n <= 16 and k >= 8 and d % 4 == 0 and _splits(bt, t_len, d, n, k, 128, 2):
+    elif 8 < n <= 16 and k >= 8 and d % 4 == 0 and split_g and _splits(bt, t_len, d, n, k, 128, 2):
         split_f = True                                    # whole-state forward, segmented
     else:
-        split_f = _splits(bt, t_len, d, n, k, 256 // g, per_sm)
+        split_f = split_g
     return 3 + 2 * split_f + 2 * split_b
 
 
