@@ -469,8 +469,8 @@ def time_bf16(lib, _native, shape, device, ins, stream, hbm_gbs, k=20):
     x, dt, dy rounded to bf16 (y, dx, ddt stored as bf16; Aneg, B, C, ckpt,
     dAneg, dB, dC fp32)."""
     bt, t_len, d, n, kk = shape
-    x, dt, aneg, b_in, c_in, dy = (t.to(torch.bfloat16) if t.dim() == 3 and t.shape[-1] == d else t
-                                   for t in ins)
+    x, dt, aneg, b_in, c_in, dy = ins
+    x, dt, dy = (t.to(torch.bfloat16) for t in (x, dt, dy))      # the channel arrays
     P = lambda t: t.data_ptr()  # noqa: E731
     y = torch.empty_like(x)
     ckpt = torch.empty(bt, (t_len + kk - 1) // kk, d, n, device=device)
@@ -519,12 +519,12 @@ def run_e2e(args, shape, device, world, rank, selective_scan, channel=False, bf1
     cd = torch.bfloat16 if bf16 else torch.float32        # channel arrays' storage
     if bf16:
         from mamba_metal import selective_scan_bf16
-        host = [t.to(cd) if t.dim() == 3 and t.shape[2] == d_total else t for t in host]
+        host = [t.to(cd) if i in (0, 1, 5) else t for i, t in enumerate(host)]   # x, dt, dy
         scan = lambda *a: selective_scan_bf16(*a, chunk=kk)  # noqa: E731
     elif channel:
         from mamba_metal.sharded import channel_shard, selective_scan_channel_sharded
         sl = channel_shard(d_total, world, rank)
-        host = [t[:, :, sl] if t.dim() == 3 and t.shape[2] == d_total else t for t in host]
+        host = [t[:, :, sl] if i in (0, 1, 5) else t for i, t in enumerate(host)]   # x, dt, dy
         host[2] = host[2][sl]
         scan = lambda *a: selective_scan_channel_sharded(*a, impl="cuda", chunk=kk)  # noqa: E731
     else:
