@@ -62,6 +62,10 @@ int mms_abi_version(void);
 /* Human-readable text for an MMS_* status. Never NULL. */
 const char *mms_status_string(int status);
 
+/* The CUDA runtime's text for the error behind the calling thread's most
+ * recent MMS_ERR_CUDA ("no error" if there was none). Never NULL. */
+const char *mms_last_cuda_error(void);
+
 /*
  * Forward scan: writes y and ckpt.
  * Replaces the reference's `lib.ssm_fwd(x, dt, aneg, b_in, c_in, y, ckpt,
@@ -212,6 +216,40 @@ int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg,
  * No counterpart in the reference (its Metal launches cannot time out).
  */
 int mms_device_status(void);
+
+/*
+ * Test hook for the failure detection above, process-wide, read by every
+ * later launch of the TMA-staged backward: `polls` is how often a thread
+ * polls a stage's completion barrier before the kernel gives up (0 restores
+ * the default, 2^22); `skip_item` >= 0 makes every CTA withhold the copies of
+ * its staged item number `skip_item` (-1: none), so that its wait runs out
+ * without any fault: the CTAs leave together after their other copies have
+ * landed, the outputs of that call are invalid, and mms_device_status()
+ * reports MMS_ERR_TIMEOUT. Not for concurrent use with production calls.
+ * No counterpart in the reference.
+ */
+int mms_debug_set_wait(unsigned int polls, int skip_item);
+
+/*
+ * Pipe-throughput probe, for the roofline the benchmark reports (the scan is
+ * bound by HBM bytes or by its exp2 count at the MUFU rate; this measures
+ * that rate on the GPU in use). Launches `blocks` CTAs of 256 threads, each
+ * thread running 8 independent chains of one operation for 2*iters rounds;
+ * per CTA it writes the elapsed SM clock cycles to cycles[cta] and the SM it
+ * ran on to sm[cta]. Operations per CTA: mms_probe_ops_per_cta(kind, iters)
+ * (thread-level; a packed FFMA2 counts as two FMAs). Keep blocks <= 4 per SM
+ * so every CTA is resident at once. `sink` needs 256 floats (never written in
+ * practice). No counterpart in the reference.
+ */
+#define MMS_PROBE_EX2 0        /* ex2.approx.ftz.f32 (MUFU)                        */
+#define MMS_PROBE_FFMA 1       /* fp32 fused multiply-add                          */
+#define MMS_PROBE_FFMA2 2      /* packed fp32 pair FMA (two lanes per instruction)  */
+#define MMS_PROBE_SHFL 3       /* warp shuffle (plus one fp32 add)                  */
+#define MMS_PROBE_EX2_POLY 4   /* the library's FMA-pipe exp2 polynomial            */
+#define MMS_PROBE_EX2_POLY2 5  /* the same on packed pairs                          */
+int mms_probe_pipe(int kind, int iters, int blocks, float *sink, long long *cycles,
+                   unsigned *sm, void *stream);
+long long mms_probe_ops_per_cta(int kind, int iters);
 
 #ifdef __cplusplus
 }

@@ -7,10 +7,22 @@
 // NULL checks.
 #include <stdint.h>
 
+#include <atomic>
+
 #include "mms_kernels.h"
 #include "mms_scan.h"
 
 namespace {
+
+// The CUDA error behind the calling thread's last MMS_ERR_CUDA (mms_last_cuda_error).
+thread_local cudaError_t g_last_cuda = cudaSuccess;
+
+int status_of(cudaError_t e)
+{
+    if (e == cudaSuccess) return MMS_OK;
+    g_last_cuda = e;
+    return MMS_ERR_CUDA;
+}
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -33,8 +45,7 @@ int fwd_impl(const float *x, const float *dt, const float *aneg, const float *B,
         !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
         return MMS_ERR_MISALIGNED;
     mms::FwdArgs a{x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, proj, 0};
-    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return status_of(mms::launch_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 
 int bwd_impl(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
@@ -55,8 +66,7 @@ int bwd_impl(const float *x, const float *dt, const float *aneg, const float *B,
     if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
     mms::BwdArgs a{x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace,
                    Bt, T, D, N, K, proj, 0};
-    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return status_of(mms::launch_bwd(a, static_cast<cudaStream_t>(stream)));
 }
 
 // Shapes the bf16 entry points cover: bf16 rows staged in 16-byte pieces
@@ -78,7 +88,19 @@ bool proj_ok(float dt_min, float dt_max)
            dt_max > dt_min;
 }
 
+std::atomic<uint32_t> g_wait_limit{0};
+std::atomic<int> g_skip_item{-1};
+
 }  // namespace
+
+namespace mms {
+uint32_t bwd_wait_limit()
+{
+    const uint32_t v = g_wait_limit.load(std::memory_order_relaxed);
+    return v ? v : (1u << 22);
+}
+int bwd_debug_skip_item() { return g_skip_item.load(std::memory_order_relaxed); }
+}  // namespace mms
 
 extern "C" {
 
@@ -92,7 +114,7 @@ const char *mms_status_string(int status)
     case MMS_ERR_UNSUPPORTED_N: return "unsupported d_state: N must be a multiple of 4 in [4, 64]";
     case MMS_ERR_WORKSPACE: return "workspace missing or smaller than mms_bwd_workspace_size()";
     case MMS_ERR_MISALIGNED: return "misaligned pointer (B, C, Aneg, ckpt, dB, dC, dAneg need 16 bytes)";
-    case MMS_ERR_CUDA: return "CUDA launch failed";
+    case MMS_ERR_CUDA: return "CUDA call failed (mms_last_cuda_error() names the CUDA error)";
     case MMS_ERR_TIMEOUT: return "a kernel timed out waiting for its staged copies (results invalid)";
     case MMS_ERR_UNSUPPORTED_BF16:
         return "bf16 scan needs D % 8 == 0 (and K == 8 for the backward)";
@@ -156,8 +178,7 @@ int mms_step(const float *x, const float *dt, const float *aneg, const float *B,
         !aligned(x, 4) || !aligned(dt, 4) || !aligned(y, 4))
         return MMS_ERR_MISALIGNED;
     mms::StepArgs a{x, dt, aneg, B, C, h, y, Bt, D, N};
-    return mms::launch_step(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                  : MMS_ERR_CUDA;
+    return status_of(mms::launch_step(a, static_cast<cudaStream_t>(stream)));
 }
 
 size_t mms_gate_workspace_size(int Bt, int T, int D)
@@ -173,9 +194,8 @@ int mms_gate_fwd(const float *y, const float *z, long long ldz, const float *d_s
         return MMS_ERR_INVALID_ARG;
     if (!aligned(y, 4) || !aligned(z, 4) || !aligned(d_skip, 4) || !aligned(out, 4))
         return MMS_ERR_MISALIGNED;
-    return mms::launch_gate_fwd(y, z, ldz, d_skip, out, (long long)Bt * T, D,
-                                static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                  : MMS_ERR_CUDA;
+    return status_of(mms::launch_gate_fwd(y, z, ldz, d_skip, out, (long long)Bt * T, D,
+                                static_cast<cudaStream_t>(stream)));
 }
 
 int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ldz,
@@ -191,10 +211,8 @@ int mms_gate_bwd(const float *dout, const float *y, const float *z, long long ld
     if (!workspace || workspace_bytes < mms::gate_workspace_bytes((long long)Bt * T, D))
         return MMS_ERR_WORKSPACE;
     if (!aligned(workspace, 16)) return MMS_ERR_MISALIGNED;
-    return mms::launch_gate_bwd(dout, y, z, ldz, d_skip, dy, dz, d_dskip, workspace,
-                                (long long)Bt * T, D, static_cast<cudaStream_t>(stream)) == cudaSuccess
-               ? MMS_OK
-               : MMS_ERR_CUDA;
+    return status_of(mms::launch_gate_bwd(dout, y, z, ldz, d_skip, dy, dz, d_dskip, workspace,
+                                (long long)Bt * T, D, static_cast<cudaStream_t>(stream)));
 }
 
 int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const float *B,
@@ -209,8 +227,7 @@ int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
         !aligned(x, 16) || !aligned(dt, 16) || !aligned(y, 16))
         return MMS_ERR_MISALIGNED;
     mms::FwdArgs a{fp(x), fp(dt), aneg, B, C, fp(y), ckpt, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
-    return mms::launch_fwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return status_of(mms::launch_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 
 int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const float *B,
@@ -232,16 +249,26 @@ int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
     if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
     mms::BwdArgs a{fp(x), fp(dt), aneg, B, C, fp(dy), ckpt, fp(dx), fp(ddt), daneg, dB, dC,
                    workspace, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
-    return mms::launch_bwd(a, static_cast<cudaStream_t>(stream)) == cudaSuccess ? MMS_OK
-                                                                                 : MMS_ERR_CUDA;
+    return status_of(mms::launch_bwd(a, static_cast<cudaStream_t>(stream)));
 }
 
 int mms_device_status(void)
 {
-    if (cudaDeviceSynchronize() != cudaSuccess) return MMS_ERR_CUDA;
-    const int t = mms::w8_take_timeout(), f = mms::fwd_take_timeout();
-    if (t < 0 || f < 0) return MMS_ERR_CUDA;
-    return t || f ? MMS_ERR_TIMEOUT : MMS_OK;
+    const cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return status_of(e);
+    const int t = mms::w8_take_timeout(), f = mms::fwd_take_timeout(), c = mms::cp_take_timeout();
+    if (t < 0 || f < 0 || c < 0) return status_of(cudaGetLastError());
+    return t || f || c ? MMS_ERR_TIMEOUT : MMS_OK;
+}
+
+const char *mms_last_cuda_error(void) { return cudaGetErrorString(g_last_cuda); }
+
+int mms_debug_set_wait(unsigned int polls, int skip_item)
+{
+    if (skip_item < -1) return MMS_ERR_INVALID_ARG;
+    g_wait_limit.store(polls, std::memory_order_relaxed);
+    g_skip_item.store(skip_item, std::memory_order_relaxed);
+    return MMS_OK;
 }
 
 }  // extern "C"

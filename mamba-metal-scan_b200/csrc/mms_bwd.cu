@@ -58,6 +58,9 @@ namespace mms {
 #ifndef MMS_BWD_MINB
 #define MMS_BWD_MINB 2
 #endif
+#ifndef MMS_BWD_CP
+#define MMS_BWD_CP 1
+#endif
 #ifndef MMS_BWD_W8
 #define MMS_BWD_W8 1
 #endif
@@ -811,7 +814,9 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
-    if (G == 4 && bwd_w8_applies(a.N, a.K) && (MMS_BWD_W8 || a.bf16)) {
+    if (G == 4 && MMS_BWD_CP && bwd_cp_applies(a)) {
+        e = launch_bwd_cp(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
+    } else if (G == 4 && bwd_w8_applies(a.N, a.K) && (MMS_BWD_W8 || a.bf16)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
         e = smem_opt_in<bwd_kernel_k8<G, VEC, PROJ, E>>(S::SMEM_K8);
@@ -830,6 +835,7 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             a.x, a.dt, a.aneg, a.B, a.C, a.dy, a.ckpt, a.dx, a.ddt, part_bc, part_a, subck, seg_e,
             a.T, a.D, a.N, a.K, w.nblk, w.nseg, sp.cps, a.proj);
     }
+    if (e != cudaSuccess) return e;                    // a launcher's own failure
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     auto blocks = [](size_t quads) {
         const size_t b = (quads + 255) / 256;

@@ -476,7 +476,7 @@ namespace {
 bool build_maps(const BwdArgs &a, W8Maps *m)
 {
     const auto fn = tma_encoder();
-    if (!fn) return false;
+    if (!fn || !tma_context()) return false;
     const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
     const cuuint32_t bX[3] = {W8_DPB, W8_CH, 1};
     const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};

@@ -26,6 +26,32 @@ __device__ __forceinline__ float ex2_fresh(float x) {
     return y;
 }
 
+// 2^x on the FMA pipe, for moving a share of the scan's exponentials off
+// MUFU. Cody and Waite's argument reduction, 2^x = 2^j * 2^f with j = round(x)
+// and f = x - j in [-1/2, 1/2] (both exact in fp32), and 2^f ~ p(f) =
+// 1 + f*q(f), q of degree 4 with coefficients from the minimax fit in
+// csrc/exp2_fit.py (max relative error of the fp32 evaluation 1.7e-7, about
+// 1.4 ulp; ex2.approx.ftz is of the same order). j is read from the low
+// mantissa bits of x + 1.5*2^23 and added to p's exponent field. x is clamped
+// to [-125, 125], so results below 2^-125 are not flushed to zero like
+// ex2.approx.ftz does, and arguments above 125 saturate instead of
+// overflowing; the scan's decays have x = -dt*Aneg*log2(e) <= 0.
+constexpr float EXP2_RND = 12582912.f;                 // 1.5 * 2^23
+constexpr float EXP2_C1 = 0x1.62e42ap-1f, EXP2_C2 = 0x1.ebf9bcp-3f, EXP2_C3 = 0x1.c6b752p-5f,
+                EXP2_C4 = 0x1.3cea7cp-7f, EXP2_C5 = 0x1.5bb9f8p-10f;
+
+__device__ __forceinline__ float ex2_poly(float x) {
+    x = fminf(fmaxf(x, -125.f), 125.f);
+    const float t = x + EXP2_RND;
+    const float f = x - (t - EXP2_RND);
+    float p = fmaf(EXP2_C5, f, EXP2_C4);
+    p = fmaf(p, f, EXP2_C3);
+    p = fmaf(p, f, EXP2_C2);
+    p = fmaf(p, f, EXP2_C1);
+    p = fmaf(p, f, 1.f);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
 // sigmoid(z) = 1 / (1 + 2^(-z*log2 e)); saturates to 0 / 1 for large |z|.
 __device__ __forceinline__ float sigmoid_fast(float z) {
     return __frcp_rn(1.f + ex2(-z * MMS_LOG2E));
@@ -64,6 +90,22 @@ __device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 ex2x2(float2 v) { return f2(ex2(v.x), ex2(v.y)); }
+
+// ex2_poly on a pair, the polynomial on packed FFMA2 (same results as two
+// ex2_poly calls: every packed operation rounds each lane as the scalar one).
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    x = f2(fminf(fmaxf(x.x, -125.f), 125.f), fminf(fmaxf(x.y, -125.f), 125.f));
+    const float2 t = add2(x, f2(EXP2_RND, EXP2_RND));
+    const float2 j = add2(t, f2(-EXP2_RND, -EXP2_RND));
+    const float2 f = fma2(j, f2(-1.f, -1.f), x);
+    float2 p = fma2(f2(EXP2_C5, EXP2_C5), f, f2(EXP2_C4, EXP2_C4));
+    p = fma2(p, f, f2(EXP2_C3, EXP2_C3));
+    p = fma2(p, f, f2(EXP2_C2, EXP2_C2));
+    p = fma2(p, f, f2(EXP2_C1, EXP2_C1));
+    p = fma2(p, f, f2(1.f, 1.f));
+    return f2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+              __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
 __device__ __forceinline__ float2 lo(float4 v) { return f2(v.x, v.y); }
 __device__ __forceinline__ float2 hi(float4 v) { return f2(v.z, v.w); }
 

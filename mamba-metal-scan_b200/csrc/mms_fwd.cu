@@ -561,7 +561,7 @@ static cudaError_t launch_fwd_s16_vb(const FwdArgs &a, const FwdMaps &maps, cuda
 static bool fwd_maps(const FwdArgs &a, FwdMaps *m)
 {
     const auto fn = tma_encoder();
-    if (!fn) return false;
+    if (!fn || !tma_context()) return false;
     const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
     const cuuint32_t bX[3] = {S16_DPB, S16_TT, 1};
     const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};

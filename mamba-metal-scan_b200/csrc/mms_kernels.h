@@ -89,6 +89,16 @@ struct SegPlan {
 
 // The shapes of the 8-state backward (mms_bwd_w8.cu): 8 < N <= 16, K == 8.
 inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8; }
+// The shapes of the channel-pair backward (mms_bwd_cp.cu): 8 < N <= 16,
+// K a multiple of 8 up to 64.
+inline bool cp_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K % 8 == 0 && K <= 64; }
+
+// Bounded waits of the TMA-staged kernels: polls of one stage's completion
+// barrier before a kernel gives up (default 2^22), and a staged item whose
+// copies are withheld (-1: none). Both are test hooks set through
+// mms_debug_set_wait (mms_api.cu); launchers read them at launch.
+uint32_t bwd_wait_limit();
+int bwd_debug_skip_item();
 
 inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
 {
@@ -100,8 +110,8 @@ inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
     // a fwd+bwd step), which pays only below one CTA per SM.
     if (base >= N_SM) return p;
     // Segments for one whole wave of the backward: the 8-state kernel runs 4
-    // CTAs per SM, the 4-state kernels (and the G-lane forward) 2. More
-    // segments than one wave holds only add local-pass work.
+    // CTAs per SM, the channel-pair and 4-state kernels (and the G-lane
+    // forward) 2. More segments than one wave holds only add local-pass work.
     const long long per_sm = w8_shape(N, K) ? 4 : 2;
     const long long want = (per_sm * N_SM) / base;
     long long cps = (nchunk + want - 1) / want;
@@ -159,6 +169,14 @@ cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const
 // 1 if a TMA-stage wait timed out since the last call (and clears it), 0 if
 // not, -1 if the flag could not be read.
 int w8_take_timeout();
+
+// Backward on channel pairs (mms_bwd_cp.cu) for cp_shape() with TMA-ready
+// arrays (D % 4 == 0 and 16-byte aligned; bf16: D % 8 == 0, no prologue);
+// same workspace regions as the general backward.
+bool bwd_cp_applies(const BwdArgs &a);
+cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                          int nblk, SegPlan sp, cudaStream_t stream);
+int cp_take_timeout();
 
 // Gate epilogue out = (y + D_skip) * silu(z) (mms_gate.cu); rows = Bt * T.
 size_t gate_workspace_bytes(long long rows, int D);

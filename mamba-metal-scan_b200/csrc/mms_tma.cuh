@@ -79,6 +79,16 @@ inline PFN_cuTensorMapEncodeTiled_v12000 tma_encoder()
     return fn;
 }
 
+// cuTensorMapEncodeTiled fails (on every map) when the calling thread has no
+// current CUDA context, which is the case on a thread that has made no CUDA
+// runtime call yet (PyTorch's autograd worker, for one). Make the current
+// device's primary context current first; cheap when it already is.
+inline bool tma_context()
+{
+    int dev = 0;
+    return cudaGetDevice(&dev) == cudaSuccess && cudaSetDevice(dev) == cudaSuccess;
+}
+
 // Tile map over a row-major array of fp32 (elem 4) or bf16 (elem 2) whose
 // innermost `rank` dims are `dim` (dim[0] contiguous), box `box`;
 // out-of-range elements load as zeros. `swz` is the shared-memory layout of a

@@ -31,6 +31,7 @@ _I = ctypes.c_int
 SIGNATURES = {
     "mms_abi_version": ([], _I),
     "mms_status_string": ([_I], ctypes.c_char_p),
+    "mms_last_cuda_error": ([], ctypes.c_char_p),
     "mms_fwd": ([_P] * 7 + [_I] * 5 + [_P], _I),
     "mms_bwd_workspace_size": ([_I] * 5, ctypes.c_size_t),
     "mms_bwd": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
@@ -46,7 +47,13 @@ SIGNATURES = {
                      + [_P], _I),
     "mms_fwd_bf16": ([_P] * 7 + [_I] * 5 + [_P], _I),
     "mms_bwd_bf16": ([_P] * 13 + [ctypes.c_size_t] + [_I] * 5 + [_P], _I),
+    "mms_debug_set_wait": ([ctypes.c_uint, _I], _I),
+    "mms_probe_pipe": ([_I] * 3 + [_P] * 4, _I),
+    "mms_probe_ops_per_cta": ([_I] * 2, ctypes.c_longlong),
 }
+
+# mms_probe_pipe kinds
+PROBE_KINDS = {"ex2": 0, "ffma": 1, "ffma2": 2, "shfl": 3, "ex2_poly": 4, "ex2_poly2": 5}
 
 _lib = None
 _lock = threading.Lock()
@@ -81,7 +88,8 @@ def status_string(rc: int) -> str:
 
 def _check(rc: int, what: str) -> None:
     if rc != MMS_OK:
-        raise RuntimeError(f"{what} failed: status {rc} ({status_string(rc)})")
+        extra = f": {load().mms_last_cuda_error().decode()}" if rc == MMS_ERR_CUDA else ""
+        raise RuntimeError(f"{what} failed: status {rc} ({status_string(rc)}){extra}")
 
 
 def _ptr(t: torch.Tensor) -> int:
@@ -225,3 +233,28 @@ def gate_bwd(dout, y, z, d_skip):
                           _ptr(dz), _ptr(dd), _ptr(ws), nb, bt, t_len, d, _stream(y.device))
     _check(rc, "mms_gate_bwd")
     return dy, dz, dd
+
+
+def pipe_rate(kind: str, device=None, iters: int = 4096, ctas_per_sm: int = 4) -> float:
+    """Operations per SM per clock of one pipe (mms_probe_pipe), measured on the
+    SM cycle counters: per SM, the operations of its CTAs over its longest CTA;
+    the median over SMs. kind: one of PROBE_KINDS."""
+    lib = load()
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    n_sm = torch.cuda.get_device_properties(device).multi_processor_count
+    blocks = n_sm * ctas_per_sm
+    sink = torch.empty(256, device=device)
+    cycles = torch.empty(blocks, dtype=torch.int64, device=device)
+    sm = torch.empty(blocks, dtype=torch.int32, device=device)
+    k = PROBE_KINDS[kind]
+    for _ in range(2):                       # the first launch warms the clocks up
+        _check(lib.mms_probe_pipe(k, iters, blocks, _ptr(sink), _ptr(cycles), _ptr(sm),
+                                  _stream(device)), "mms_probe_pipe")
+    torch.cuda.synchronize(device)
+    ops = int(lib.mms_probe_ops_per_cta(k, iters))
+    per_sm = {}
+    for c, s in zip(cycles.tolist(), sm.tolist()):
+        n, m = per_sm.get(s, (0, 0))
+        per_sm[s] = (n + 1, max(m, c))
+    rates = sorted(n * ops / m for n, m in per_sm.values())
+    return rates[len(rates) // 2]

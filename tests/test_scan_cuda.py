@@ -353,3 +353,31 @@ def test_no_kernel_reported_a_timeout():
     x, dt, aneg, b_in, c_in, dy = inputs(16, 512, 2304, 16, "c0", seed=9, device=DEV)
     cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=8)
     assert _native.device_status() == _native.MMS_OK
+
+
+def test_backward_from_a_fresh_thread_matches_the_float64_oracle():
+    """The first scan on a thread that has made no CUDA call yet (as PyTorch's
+    autograd worker is at its first backward): the kernels' TMA tensor maps
+    need the device's context made current on that thread."""
+    import threading
+    from mamba_metal import _native
+    x, dt, aneg, b_in, c_in, dy = inputs(2, 64, 32, 16, "ref", seed=SEED + 7, device=DEV)
+    out = {}
+
+    def run():
+        try:
+            for chunk in (64, 8):
+                y, ckpt = _native.fwd(x, dt, aneg, b_in, c_in, chunk)
+                out[chunk] = (y, _native.bwd(x, dt, aneg, b_in, c_in, dy, ckpt, chunk))
+            torch.cuda.synchronize()
+        except Exception as e:          # surfaced in the main thread below
+            out["error"] = e
+
+    th = threading.Thread(target=run)
+    th.start()
+    th.join()
+    assert "error" not in out, out.get("error")
+    y64, _, g64 = oracle64(x, dt, aneg, b_in, c_in, dy)
+    for chunk in (64, 8):
+        y, grads = out[chunk]
+        assert_parity(y, grads, y64, g64, f"fresh thread, chunk {chunk}")
