@@ -63,6 +63,10 @@
 #ifndef MMS_BWD_CP_MINB
 #define MMS_BWD_CP_MINB 2
 #endif
+// K = 8 runs the 8-state kernel (mms_bwd_w8.cu) unless this is set.
+#ifndef MMS_BWD_CP_K8
+#define MMS_BWD_CP_K8 0
+#endif
 
 namespace mms {
 
@@ -92,7 +96,7 @@ struct CpSmem {
     static constexpr int SLOT = CP_THREADS * 8;             // one entry state per thread
     template <typename E>
     static size_t bytes(int m) {
-        return sizeof(float) * ((size_t)CP_NAT * CpTile<E>::F + 2 * CP_SUB * 128 + SD + (size_t)(m - 1) * SLOT) + 64;
+        return sizeof(float) * ((size_t)CP_NAT * CpTile<E>::F + 2 * CP_SUB * 64 + SD + (size_t)(m - 1) * SLOT) + 64;
     }
 };
 
@@ -117,15 +121,14 @@ __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16 *p) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
 }
 
-// Per-thread constants. Every float2 of a thread pairs its two channels
-// (channel 0, channel 1) for one state, so the per-channel step inputs
-// (dt, x, dy and dt*x) are natural pairs and only B and C, which are per
-// state, need both lanes equal: they come pre-duplicated from shared memory.
+// Per-thread constants. The arithmetic is scalar: packed FFMA2 / FMUL2 add no
+// FP32 throughput on this GPU (measured 122.6 vs 123.8 lanes per clock per
+// SM) and their register-pair operands cost moves.
 struct CpLane {
     int lane, q, tau, pr;
     int d0c;                      // channel 0 of the pair
     bool dv0, dv1;
-    float2 nan[4];                // -Aneg*log2(e) of state s(m), (channel 0, channel 1)
+    float nan[4][2];              // -Aneg*log2(e) of state s(m), [m][channel]
     __device__ CpLane(const float *aneg, int D, int N, bool proj) {
         const int tid = threadIdx.x;
         lane = tid & 31;
@@ -138,71 +141,71 @@ struct CpLane {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
             const int s = state(m);
-            float a0 = dv0 && s < N ? __ldg(aneg + (size_t)d0c * N + s) : 0.f;
-            float a1 = dv1 && s < N ? __ldg(aneg + (size_t)(d0c + 1) * N + s) : 0.f;
-            if (proj) {
-                a0 = dv0 && s < N ? softplus(a0) : 0.f;
-                a1 = dv1 && s < N ? softplus(a1) : 0.f;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+                const bool ok = (c ? dv1 : dv0) && s < N;
+                float a = ok ? __ldg(aneg + (size_t)(d0c + c) * N + s) : 0.f;
+                if (proj) a = ok ? softplus(a) : 0.f;
+                nan[m][c] = -a * MMS_LOG2E;
             }
-            nan[m] = f2(-a0 * MMS_LOG2E, -a1 * MMS_LOG2E);
         }
     }
     __device__ int state(int m) const { return 4 * q + (m ^ tau); }
 };
 
-// One thread's 8 state values: [position m] = (channel 0, channel 1) of state s(m).
+// One thread's 8 state values: [position m (state s(m))][channel].
 struct St8 {
-    float2 v[4];
+    float v[4][2];
 };
 
-// Shared-memory layout of B and C duplicated per state, in the four lane
-// state orders: [a (B, C)][t][half][tau][q][4] with (B_s(2h), B_s(2h), B_s(2h+1),
-// B_s(2h+1)) at [.. half = h ..]; a warp's 16-byte reads of one half touch 16
-// consecutive 16-byte pieces (no bank conflicts).
-constexpr int CP_DUP_STEP = 2 * 4 * 4 * 4;              // floats per step and array
-constexpr int CP_DUP = 2 * CP_SUB * CP_DUP_STEP;        // both arrays, 2048 floats
+// B and C rows of the 8 steps in the four lane state orders,
+// [a (B, C)][t][tau][16]: (B_s(0), .., B_s(3)) of lane (q, tau) at [..][tau][4q].
+constexpr int CP_PERM = 2 * CP_SUB * 4 * 16;
 
 template <typename E>
 struct CpView {
     const E *x, *dt, *dy;        // channel pair of this lane, step stride CP_DPB
-    const float *B, *C;          // dup rows of this lane: step stride CP_DUP_STEP
+    const float *B, *C;          // this lane's permuted rows, step stride 64
     const float *ck;             // entry slab [64][16]
-    __device__ CpView(const float *st, const float *dup, const CpLane &L) {
+    __device__ CpView(const float *st, const float *perm, const CpLane &L) {
         x = reinterpret_cast<const E *>(st) + 2 * L.pr;
         dt = reinterpret_cast<const E *>(st + CpTile<E>::ARR) + 2 * L.pr;
         dy = reinterpret_cast<const E *>(st + 2 * CpTile<E>::ARR) + 2 * L.pr;
-        B = dup + L.tau * 16 + 4 * L.q;
-        C = B + CP_SUB * CP_DUP_STEP;
+        B = perm + L.tau * 16 + 4 * L.q;
+        C = B + CP_SUB * 64;
         ck = st + CpTile<E>::CK;
     }
     __device__ float2 xs(int t) const { return ld_pair(x + t * CP_DPB); }
     __device__ float2 dts(int t) const { return ld_pair(dt + t * CP_DPB); }
     __device__ float2 dys(int t) const { return ld_pair(dy + t * CP_DPB); }
-    // (B_s(2h), B_s(2h), B_s(2h+1), B_s(2h+1))
-    __device__ float4 Bs(int t, int h) const { return *reinterpret_cast<const float4 *>(B + t * CP_DUP_STEP + h * 64); }
-    __device__ float4 Cs(int t, int h) const { return *reinterpret_cast<const float4 *>(C + t * CP_DUP_STEP + h * 64); }
+    __device__ float4 Bs(int t) const { return *reinterpret_cast<const float4 *>(B + t * 64); }
+    __device__ float4 Cs(int t) const { return *reinterpret_cast<const float4 *>(C + t * 64); }
     // the chunk's entry state from the checkpoint slab
     __device__ void entry(St8 &h, const CpLane &L) const {
         const float *r0 = ck + (2 * L.pr) * 16, *r1 = r0 + 16;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) h.v[m] = f2(r0[L.state(m)], r1[L.state(m)]);
+        for (int m = 0; m < 4; ++m) {
+            h.v[m][0] = r0[L.state(m)];
+            h.v[m][1] = r1[L.state(m)];
+        }
     }
 };
 
-__device__ __forceinline__ float2 dup_of(const float4 &lo4, const float4 &hi4, int m) {
-    return m == 0 ? lo(lo4) : m == 1 ? hi(lo4) : m == 2 ? lo(hi4) : hi(hi4);
-}
+__device__ __forceinline__ float cpt(const float2 &v, int c) { return c ? v.y : v.x; }
 
 // h <- one step; the step's dA returned in dA.
 template <typename E>
 __device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E> &v, const CpLane &L, int t) {
-    const float2 dt2 = v.dts(t);
-    const float2 bx2 = mul2(dt2, v.xs(t));
-    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
+    const float2 dt2 = v.dts(t), x2 = v.xs(t);
+    const float4 Bv = v.Bs(t);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        dA.v[m] = ex2x2(mul2(dt2, L.nan[m]));
-        h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, dup_of(B0, B1, m)));
+    for (int c = 0; c < 2; ++c) {
+        const float dtc = cpt(dt2, c), bx = dtc * cpt(x2, c);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            dA.v[m][c] = ex2(dtc * L.nan[m][c]);
+            h.v[m][c] = fmaf(dA.v[m][c], h.v[m][c], bx * comp(Bv, m));
+        }
     }
 }
 
@@ -215,30 +218,33 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
                                              const Proj &pj)
 {
     const float2 dt2 = v.dts(t), x2 = v.xs(t), dy2 = v.dys(t);
-    const float2 bx2 = mul2(dt2, x2);
-    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1), C0 = v.Cs(t, 0), C1 = v.Cs(t, 1);
-    float2 sB, sA, P[4];                  // P[m] = (sum over the pair of g*dt*x, of dy*h_t)
+    const float4 Bv = v.Bs(t), Cv = v.Cs(t);
+    float sB[2], sA[2], vb[4], vc[4];
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const float2 g = fma2(dy2, dup_of(C0, C1, m), r.v[m]);
-        const float2 rn = mul2(dA.v[m], g);
-        const float2 u = mul2(rn, hp.v[m]);
-        sB = m ? fma2(g, dup_of(B0, B1, m), sB) : mul2(g, dup_of(B0, B1, m));
-        sA = m ? fma2(L.nan[m], u, sA) : mul2(L.nan[m], u);
-        dac.v[m] = fma2(dt2, u, dac.v[m]);
-        const float2 pb = mul2(g, bx2), pc = mul2(dy2, hc.v[m]);
-        P[m] = f2(pb.x + pb.y, pc.x + pc.y);
-        r.v[m] = rn;
+    for (int c = 0; c < 2; ++c) {
+        const float dtc = cpt(dt2, c), dyc = cpt(dy2, c), bx = dtc * cpt(x2, c);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+            const float g = fmaf(dyc, comp(Cv, m), r.v[m][c]);
+            const float rn = dA.v[m][c] * g;
+            const float u = rn * hp.v[m][c];
+            sB[c] = m ? fmaf(g, comp(Bv, m), sB[c]) : g * comp(Bv, m);
+            sA[c] = m ? fmaf(L.nan[m][c], u, sA[c]) : L.nan[m][c] * u;
+            dac.v[m][c] = fmaf(dtc, u, dac.v[m][c]);
+            vb[m] = c ? fmaf(bx, g, vb[m]) : bx * g;
+            vc[m] = c ? fmaf(dyc, hc.v[m][c], vc[m]) : dyc * hc.v[m][c];
+            r.v[m][c] = rn;
+        }
     }
     {   // dx = dt*sum gB, ddt = x*sum gB + ln2*sum nan*u, over the pair's 4 state lanes
-        const float2 pdx = mul2(dt2, sB);
-        const float2 pddt = fma2(x2, sB, mul2(f2(CP_LN2, CP_LN2), sA));
+        const float dx0 = dt2.x * sB[0], dx1 = dt2.y * sB[1];
+        const float dd0 = fmaf(x2.x, sB[0], CP_LN2 * sA[0]), dd1 = fmaf(x2.y, sB[1], CP_LN2 * sA[1]);
         const bool b0 = L.lane & 1, b1 = (L.lane >> 1) & 1;
-        float2 keep = b0 ? f2(pdx.y, pddt.y) : f2(pdx.x, pddt.x);
-        const float2 send = b0 ? f2(pdx.x, pddt.x) : f2(pdx.y, pddt.y);
-        keep = add2(keep, shfl2(send, 1));
-        float kv = b1 ? keep.y : keep.x;
-        kv += __shfl_xor_sync(0xffffffffu, b1 ? keep.x : keep.y, 2);
+        float kx = b0 ? dx1 : dx0, kd = b0 ? dd1 : dd0;
+        kx += __shfl_xor_sync(0xffffffffu, b0 ? dx0 : dx1, 1);
+        kd += __shfl_xor_sync(0xffffffffu, b0 ? dd0 : dd1, 1);
+        float kv = b1 ? kd : kx;
+        kv += __shfl_xor_sync(0xffffffffu, b1 ? kx : kd, 2);
         // this lane ends with channel b0, kind b1 (0 dx, 1 ddt); outp points at
         // its own output array and channel
         if (PROJ && b1) {
@@ -248,12 +254,15 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
         if (t < nv && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
     }
     // dB | dC over the warp's 8 channel pairs: lane bits 4, 3 select-free, bit 2 by kind
-    P[0] = add2(P[0], shfl2(P[2], 16));
-    P[1] = add2(P[1], shfl2(P[3], 16));
-    P[0] = add2(P[0], shfl2(P[1], 8));
+    vb[0] += __shfl_xor_sync(0xffffffffu, vb[2], 16);
+    vb[1] += __shfl_xor_sync(0xffffffffu, vb[3], 16);
+    vc[0] += __shfl_xor_sync(0xffffffffu, vc[2], 16);
+    vc[1] += __shfl_xor_sync(0xffffffffu, vc[3], 16);
+    vb[0] += __shfl_xor_sync(0xffffffffu, vb[1], 8);
+    vc[0] += __shfl_xor_sync(0xffffffffu, vc[1], 8);
     const int kb = (L.lane >> 2) & 1;
-    float kk = kb ? P[0].y : P[0].x;
-    kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 4);
+    float kk = kb ? vc[0] : vb[0];
+    kk += __shfl_xor_sync(0xffffffffu, kb ? vb[0] : vc[0], 4);
     sd[(t * CP_WARPS + warp) * 32 + kb * 16 + L.state(0)] = kk;
 }
 
@@ -268,30 +277,57 @@ __device__ __forceinline__ void cp_entry(St8 &h, const CpView<E> &v, const CpLan
     } else {
         const float4 a0 = reinterpret_cast<const float4 *>(slot_in)[0];
         const float4 a1 = reinterpret_cast<const float4 *>(slot_in)[1];
-        h.v[0] = lo(a0);
-        h.v[1] = hi(a0);
-        h.v[2] = lo(a1);
-        h.v[3] = hi(a1);
+        h.v[0][0] = a0.x; h.v[0][1] = a0.y; h.v[1][0] = a0.z; h.v[1][1] = a0.w;
+        h.v[2][0] = a1.x; h.v[2][1] = a1.y; h.v[3][0] = a1.z; h.v[3][1] = a1.w;
     }
 }
 
-// Rebuild (all states and decays of the 8 steps kept) and walk a sub-chunk
-// (nv valid steps) from its entry state and carry r.
+// h <- one step with a known dA (no ex2).
+template <typename E>
+__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E> &v, int t) {
+    const float2 dt2 = v.dts(t), x2 = v.xs(t);
+    const float4 Bv = v.Bs(t);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const float bx = cpt(dt2, c) * cpt(x2, c);
+#pragma unroll
+        for (int m = 0; m < 4; ++m) h.v[m][c] = fmaf(dA.v[m][c], h.v[m][c], bx * comp(Bv, m));
+    }
+}
+
+// Rebuild and walk a sub-chunk (nv valid steps) from its entry state and
+// carry r. All 8 decays are kept; of the states only h_4..h_7, and h_{-1}..h_3
+// are recomputed from the entry state with the kept decays (no ex2) when the
+// walk reaches them, which keeps the live registers low.
 template <typename E, bool PROJ>
 __device__ __forceinline__ void cp_walk(const CpView<E> &v, const CpLane &L, int j,
                                         const float *slot_in, St8 &r, St8 &dac, int nv, E *outp,
                                         int D, float *sd, int warp, const Proj &pj)
 {
-    St8 dA[CP_SUB], h[CP_SUB + 1];        // h[t + 1] = h_t, h[0] = entry
-    cp_entry<E>(h[0], v, L, j, slot_in);
+    St8 dA[CP_SUB], hk[4];                // hk[t - 4] = h_t
+    {
+        St8 h;
+        cp_entry<E>(h, v, L, j, slot_in);
 #pragma unroll
-    for (int t = 0; t < CP_SUB; ++t) {
-        h[t + 1] = h[t];
-        cp_advance<E>(h[t + 1], dA[t], v, L, t);
+        for (int t = 0; t < CP_SUB; ++t) {
+            cp_advance<E>(h, dA[t], v, L, t);
+            if (t >= 4) hk[t - 4] = h;
+        }
     }
 #pragma unroll
-    for (int t = CP_SUB - 1; t >= 0; --t)
-        cp_walk_step<E, PROJ>(v, L, h[t + 1], h[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+    for (int t = CP_SUB - 1; t >= 5; --t)
+        cp_walk_step<E, PROJ>(v, L, hk[t - 4], hk[t - 5], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+    St8 hl[5];                            // hl[t + 1] = h_t for t = -1 .. 3
+    cp_entry<E>(hl[0], v, L, j, slot_in);
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+        hl[t + 1] = hl[t];
+        cp_replay<E>(hl[t + 1], dA[t], v, t);
+    }
+    cp_walk_step<E, PROJ>(v, L, hk[0], hl[4], dA[4], r, dac, 4, nv, outp, D, sd, warp, pj);
+#pragma unroll
+    for (int t = 3; t >= 0; --t)
+        cp_walk_step<E, PROJ>(v, L, hl[t + 1], hl[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
 }
 
 // The item sequence of one CTA: chunks chi down to clo; in a chunk with mv
@@ -335,8 +371,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     using Q = CpTile<E>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;                                  // [CP_NAT][Q::F]
-    float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (CP_DUP)
-    float *sd = dup + CP_DUP;                              // [8][4][32]
+    float *perm = stages + CP_NAT * Q::F;                  // B, C in the lane orders (CP_PERM)
+    float *sd = perm + CP_PERM;                            // [8][4][32]
     float *slots = sd + CpSmem::SD;                        // [M-1][128][8]
     const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * CpSmem::SLOT);
 
@@ -372,13 +408,14 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 
     St8 r, dac;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) r.v[m] = dac.v[m] = f2(0.f, 0.f);
+    for (int m = 0; m < 4; ++m) r.v[m][0] = r.v[m][1] = dac.v[m][0] = dac.v[m][1] = 0.f;
     if (sg + 1 < nsg) {                                    // adjoint carry from the later segments
         const float *src = seg_e + ((size_t)brow * nsg + sg) * plane + (size_t)L.d0c * N;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
             const int s = L.state(m);
-            r.v[m] = f2(L.dv0 && s < N ? src[s] : 0.f, L.dv1 && s < N ? src[N + s] : 0.f);
+            r.v[m][0] = L.dv0 && s < N ? src[s] : 0.f;
+            r.v[m][1] = L.dv1 && s < N ? src[N + s] : 0.f;
         }
     }
 
@@ -423,13 +460,12 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
             flush(pend_t0, pend_nv);
             pend_t0 = -1;
         }
-        // B, C of the 8 steps duplicated per state in the four lane orders
-        for (int e = tid; e < 2 * CP_SUB * 2 * 4 * 4; e += CP_THREADS) {
-            const int qq = e & 3, ta = (e >> 2) & 3, hh = (e >> 4) & 1, t = (e >> 5) & 7, a = e >> 8;
+        // B, C of the 8 steps in the four lane state orders: perm[a][t][tau][16]
+        for (int e = tid; e < 2 * CP_SUB * 4 * 4; e += CP_THREADS) {
+            const int qq = e & 3, ta = (e >> 2) & 3, t = (e >> 4) & 7, a = e >> 7;
             const float *src = st + Q::BC + (a * CP_SUB + t) * 16 + 4 * qq;
-            const float b0 = src[(2 * hh) ^ ta], b1 = src[(2 * hh + 1) ^ ta];
-            *reinterpret_cast<float4 *>(dup + (a * CP_SUB + t) * CP_DUP_STEP + ((hh * 4 + ta) * 4 + qq) * 4) =
-                make_float4(b0, b0, b1, b1);
+            *reinterpret_cast<float4 *>(perm + ((a * CP_SUB + t) * 4 + ta) * 16 + 4 * qq) =
+                make_float4(src[0 ^ ta], src[1 ^ ta], src[2 ^ ta], src[3 ^ ta]);
         }
         if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
             float *dts = st + Q::ARR;
@@ -442,7 +478,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         }
         __syncthreads();
 
-        const CpView<E> v(st, dup, L);
+        const CpView<E> v(st, perm, L);
         const int u = c * M + j;                           // sub-chunk index in the sequence
         const int t0 = u * CP_SUB;
         const int nv = min(CP_SUB, T - t0);
@@ -454,8 +490,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 #pragma unroll
             for (int t = 0; t < CP_SUB; ++t) cp_advance<E>(h, dA, v, L, t);
             float4 *sl = reinterpret_cast<float4 *>(slots + (size_t)j * CpSmem::SLOT + tid * 8);
-            sl[0] = make_float4(h.v[0].x, h.v[0].y, h.v[1].x, h.v[1].y);
-            sl[1] = make_float4(h.v[2].x, h.v[2].y, h.v[3].x, h.v[3].y);
+            sl[0] = make_float4(h.v[0][0], h.v[0][1], h.v[1][0], h.v[1][1]);
+            sl[1] = make_float4(h.v[2][0], h.v[2][1], h.v[3][0], h.v[3][1]);
         } else {
             // this lane's output after the dx / ddt exchange: array (lane bit 1), channel (bit 0)
             E *outp = ((L.lane >> 1) & 1 ? ddt : dx) + rowD + (size_t)t0 * D + L.d0c + (L.lane & 1);
@@ -471,8 +507,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     for (int m = 0; m < 4; ++m) {
         const int s = L.state(m);
         if (s < N) {
-            if (L.dv0) pa[s] = -dac.v[m].x;
-            if (L.dv1) pa[N + s] = -dac.v[m].y;
+            if (L.dv0) pa[s] = -dac.v[m][0];
+            if (L.dv1) pa[N + s] = -dac.v[m][1];
         }
     }
 }
@@ -515,7 +551,7 @@ cudaError_t launch_cp(const BwdArgs &a, float *part_bc, float *part_a, const flo
 
 bool bwd_cp_applies(const BwdArgs &a)
 {
-    if (!cp_shape(a.N, a.K) || a.K == CP_SUB) return false;    // K = 8: the 8-state kernel
+    if (!cp_shape(a.N, a.K) || (a.K == CP_SUB && !MMS_BWD_CP_K8)) return false;
 
     if (a.bf16) return false;              // bf16 stays on the 8-state kernel (mms_bwd_w8.cu)
     return vec_ok(a.D, a.x, a.dt, a.dy);
