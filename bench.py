@@ -12,8 +12,15 @@ scans its own batch (batch sharding, no collective: weak scaling) and `value`
 is the total elements of all ranks over the slowest rank's device time.
 
 Printed (rank 0): one JSON line with the contract keys plus
-  roofline      the dominant kernel (mms_bwd) against measured HBM bandwidth,
-                and `step_roofline`: max(HBM time, MUFU ex2 time) / step time
+  pipe_rates    ex2 (MUFU), FFMA, shuffle and FMA-pipe exp2 throughput per SM
+                per clock, measured in this run (mms_probe_pipe)
+  roofline      the dominant kernel (mms_bwd) against its binding limit, the
+                slower of its algorithmic HBM bytes and its exp2 count at the
+                measured MUFU rate; `step_roofline`: the same for fwd + bwd
+  stride64      the same step at the reference's checkpoint stride (64),
+                with its own roofline
+  c4_channel_shard  config 4 with d_inner split over the N GPUs and one NCCL
+                all-reduce of the packed [dB|dC] partials (timed on its own)
   cpu_baseline  the reference's CPU path (oracle/ref_torch.py) on a bounded
                 sample, host threads stated
   e2e           the public API (selective_scan + autograd) from pinned host
@@ -24,7 +31,8 @@ Printed (rank 0): one JSON line with the contract keys plus
   gate          the block's (y + D) * silu(z) epilogue, one kernel each way
   bf16          the scan kernels with bf16 x, dt, y, dy, dx, ddt (fp32 arithmetic)
   clocks        nvidia-smi samples taken during the timed region
-`--impl reference` times only the reference CPU path (rank 0) and prints its line.
+`--impl reference` times only the reference CPU path (rank 0) on the full
+per-GPU workload each step and prints its line with the same `config`.
 """
 from __future__ import annotations
 
@@ -48,8 +56,11 @@ import torch.distributed as dist  # noqa: E402
 
 METRIC = "scan fwd+bwd B*T*D elems/s"
 UNIT = "elem/s"
-MUFU_EX2_PER_CLK_SM = 16.0      # measured on this pool's B200 (ex2.approx.f32 throughput)
 N_SM = 148
+# FP32 lanes the backward needs per state-step at the least: the rebuild (the
+# decay's exponent product, dt*x*B and the state update) and the walk (the
+# adjoint update, dA*g, u = dA*g*h, and the sums for dx, ddt, dAneg, dB, dC).
+BWD_FP32_LANES_PER_STATE_STEP = 11
 
 CONFIGS = {
     # name: (B, T, D, N, K)
@@ -87,6 +98,47 @@ def launches_per_step(bt, t_len, d, n, k):
     else:
         split_f = split_g
     return 3 + 2 * split_f + 2 * split_b
+
+
+def workload_config(name, shape, world, channel, d_local):
+    """The `config` object both arms print (the driver compares them key by key)."""
+    bt, t_len, d_total, n, kk = shape
+    btd = bt * t_len * d_total
+    touched = (32 * btd + 24 * bt * t_len * n + 12 * d_total * n) / 1e6
+    return {"workload": (f"{name}: scan fwd+bwd B{bt} T{t_len} D{d_total} N{n} K{kk}, "
+                         f"d_inner sharded {d_local} per GPU" if channel else
+                         f"{name}: scan fwd+bwd B{bt} T{t_len} D{d_total} N{n} K{kk} per GPU"),
+            "batch_per_gpu": bt, "seq_len": t_len, "d_inner": d_total, "d_state": n, "chunk": kk,
+            "parallelism": (f"d_inner-shard x{world} + NCCL all-reduce of packed [dB|dC] "
+                            f"({2 * bt * t_len * n * 4} B)" if channel else
+                            f"batch-shard x{world} (no collective)"),
+            "l2": "inputs larger than L2 (%.0f MB touched per step per GPU)" % touched}
+
+
+def pipe_rates(device):
+    """Operations per SM per clock measured on this GPU (mms_probe_pipe)."""
+    from mamba_metal import _native
+    return {k: round(_native.pipe_rate(k, device), 2) for k in ("ex2", "ffma", "ffma2", "shfl", "ex2_poly2")}
+
+
+def kernel_roofline(name, t_s, nbytes, exps, hbm_gbs, ex2_per_s, fp32_lanes=None, ffma_per_s=None):
+    """A kernel against the slower of its HBM bytes and its exp2 count at the
+    measured MUFU rate; the FP32-pipe time of its minimum lanes beside them."""
+    t_hbm, t_mufu = nbytes / (hbm_gbs * 1e9), exps / ex2_per_s
+    mufu = t_mufu >= t_hbm
+    out = {"kernel": name, "bound": "mufu" if mufu else "hbm",
+           "achieved": exps / t_s / 1e9 if mufu else nbytes / t_s / 1e9,
+           "peak": ex2_per_s / 1e9 if mufu else hbm_gbs,
+           "unit": "G exp2/s" if mufu else "GB/s",
+           "frac": max(t_hbm, t_mufu) / t_s,
+           "t_hbm_us": t_hbm * 1e6, "t_mufu_us": t_mufu * 1e6, "t_kernel_us": t_s * 1e6,
+           "hbm": {"achieved_gbs": nbytes / t_s / 1e9, "frac": t_hbm / t_s,
+                   "algorithmic_bytes_per_launch": nbytes},
+           "exps_per_launch": exps}
+    if fp32_lanes is not None:
+        t_fp = fp32_lanes / ffma_per_s
+        out["fp32_pipe"] = {"min_lanes_per_launch": fp32_lanes, "t_us": t_fp * 1e6, "frac": t_fp / t_s}
+    return out
 
 
 def make_inputs(bt, t_len, d, n, seed, device):
@@ -210,65 +262,54 @@ def barrier(world):
 
 # ------------------------------------------------------------- CPU reference
 
-def reference_slice(shape, budget_s: float, seed: int = 0) -> int:
-    """Channels of `shape` whose reference fwd+bwd takes about `budget_s` on this host."""
+def time_reference_steps(shape, steps: int, budget_s: float, seed: int = 1000):
+    """The reference's CPU path (oracle/ref_torch.fwd_bwd: the reference's
+    impl='torch' forward + autograd backward) on the full per-GPU workload,
+    all host threads: one untimed warm-up step, then up to `steps` timed steps,
+    fewer if the warm-up says they would take longer than `budget_s`."""
     from oracle import ref_torch
     bt, t_len, d, n, _ = shape
-    probe_d = min(d, 32)
-    ins = make_inputs(bt, t_len, probe_d, n, seed, "cpu")
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ins = make_inputs(bt, t_len, d, n, seed, "cpu")
     t0 = time.perf_counter()
     ref_torch.fwd_bwd(*ins)
-    probe = time.perf_counter() - t0
-    return max(1, min(d, int(probe_d * budget_s / max(probe, 1e-6))))
-
-
-def time_reference_cpu(shape, ds: int, seed: int = 0):
-    """The reference's CPU path (oracle/ref_torch.fwd_bwd) on a D-slice of `shape`.
-
-    Every channel is an independent recurrence and the work per element is the
-    same in a slice, so elements/s of the slice stands for the full shape.
-    """
-    from oracle import ref_torch
-    bt, t_len, d, n, _ = shape
-    threads = torch.get_num_threads()
-    ins = make_inputs(bt, t_len, ds, n, seed, "cpu")
-    t0 = time.perf_counter()
-    ref_torch.fwd_bwd(*ins)
-    el = time.perf_counter() - t0
-    elems = bt * t_len * ds
-    return {"value": elems / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"reference impl='torch' (oracle/ref_torch.py) fwd + autograd bwd on "
-                      f"B{bt} T{t_len} D{ds} of {d} channels, N{n}: {elems} elems in {el:.2f} s, "
+    t_warm = time.perf_counter() - t0
+    n_timed = max(1, min(steps, int(budget_s / max(t_warm, 1e-6))))
+    times = []
+    for _ in range(n_timed):
+        t0 = time.perf_counter()
+        ref_torch.fwd_bwd(*ins)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    elems = bt * t_len * d
+    return {"value": elems * n_timed / total, "unit": UNIT, "cores": threads, "kind": "port",
+            "steps": n_timed, "warmup": 1, "ms_per_step": 1e3 * total / n_timed,
+            "sample": f"reference impl='torch' (oracle/ref_torch.py) fwd + autograd bwd on the full "
+                      f"B{bt} T{t_len} D{d} N{n} workload, {n_timed} timed step(s) after 1 warm-up, "
                       f"{threads} torch CPU threads"}
 
 
 def cpu_baseline(shape, budget_s: float):
-    torch.set_num_threads(os.cpu_count() or 1)
-    return time_reference_cpu(shape, reference_slice(shape, budget_s))
+    return time_reference_steps(shape, 1000, budget_s)
 
 
 def run_reference(args, shape):
     world, rank, _ = dist_setup()
     if rank != 0:
         return
-    torch.set_num_threads(os.cpu_count() or 1)
-    k, w = args.steps, args.warmup
-    budget = max(0.05, min(20.0, 120.0 / max(1, k + w)))     # whole run within ~2 minutes
-    ds = reference_slice(shape, budget)
-    results = [time_reference_cpu(shape, ds, seed=s) for s in range(w + k)]
-    timed = results[w:]
-    value = statistics.median(r["value"] for r in timed)
-    bt, t_len, d, n, kk = shape
+    r = time_reference_steps(shape, args.steps, args.ref_budget)
+    channel = args.shard == "channel" and world > 1
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
-        "n_gpus": args.gpus, "steps": k, "warmup": w,
-        "ms_per_step": 1e3 * bt * t_len * d / value, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d} N{n} K{kk}",
-                   "batch": bt, "seq_len": t_len, "d_inner": d, "d_state": n, "chunk": kk,
-                   "parallelism": "CPU, rank 0 only"},
-        "cpu_baseline": dict(timed[-1], value=value),
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "impl": "reference", "metric": METRIC, "value": r["value"], "unit": UNIT,
+        "n_gpus": args.gpus, "steps": r["steps"], "warmup": r["warmup"],
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if channel else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": workload_config(args.config, shape, world, channel,
+                                  shape[2] // world if channel else shape[2]),
+        "cpu_baseline": dict((k, r[k]) for k in ("value", "unit", "cores", "kind", "sample")),
+        "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     print(json.dumps(line), flush=True)
@@ -286,6 +327,7 @@ def run_native(args, shape):
         dist.init_process_group("nccl", device_id=device,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     lib = _native.load()
+    rates = pipe_rates(device)
     bt, t_len, d_total, n, kk = shape
     channel = args.shard == "channel" and world > 1
     if channel:
@@ -356,59 +398,61 @@ def run_native(args, shape):
 
     hbm_gbs, peak_kind, sm_max_default = measured_peaks()
     clk = clocks.summary()
+    sm_mhz = clk.get("sm_mhz") or sm_max_default
     fwd_b, bwd_b = algorithmic_bytes(bt, t_len, d, n)
-    achieved = bwd_b / (bwd_ms * 1e-3) / 1e9
+    # per-SM rates measured on this GPU, at the median SM clock of the timed region
+    ex2_per_s = rates["ex2"] * N_SM * sm_mhz * 1e6
+    ffma_per_s = rates["ffma"] * N_SM * sm_mhz * 1e6
+    bdn = elems * n                                         # state elements per pass
     traffic = None
     tfile = REPO / "profiles" / "traffic.json"
-    if tfile.exists():
-        if kk == 8:           # the capture was taken at the default stride
-            traffic = json.loads(tfile.read_text()).get(f"{args.config}_bwd_bytes_per_launch")
-    sm_mhz = clk.get("sm_mhz") or sm_max_default
-    exps = 2 * elems * n
-    t_hbm = (fwd_b + bwd_b) / (hbm_gbs * 1e9)
-    t_mufu = exps / (MUFU_EX2_PER_CLK_SM * N_SM * sm_mhz * 1e6)
-    t_mufu_max = exps / (MUFU_EX2_PER_CLK_SM * N_SM * sm_max_default * 1e6)
+    if tfile.exists() and kk == 8:                          # captured at the default stride
+        traffic = json.loads(tfile.read_text()).get(f"{args.config}_bwd_bytes_per_launch")
+    roof = kernel_roofline("mms_bwd (bwd_kernel_w8 + reduce_kernel)" if kk == 8 else
+                           "mms_bwd (bwd_kernel_cp + reduce_kernel)", bwd_ms * 1e-3, bwd_b, bdn,
+                           hbm_gbs, ex2_per_s, BWD_FP32_LANES_PER_STATE_STEP * bdn, ffma_per_s)
+    roof["traffic"] = traffic
+    roof["peak_source"] = (f"HBM: {peak_kind} (MEASURED_PEAKS.json hbm_gbs); MUFU: measured in this "
+                           f"run, {rates['ex2']} ex2/clk/SM x {N_SM} SMs x {sm_mhz:.0f} MHz")
     t_step = ms_per_step * 1e-3 if world == 1 else local_ms * 1e-3 / K
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong" if channel else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
-        "config": {"workload": (f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d_total} N{n} K{kk}, "
-                                f"d_inner sharded {d} per GPU" if channel else
-                                f"{args.config}: scan fwd+bwd B{bt} T{t_len} D{d} N{n} K{kk} per GPU"),
-                   "batch_per_gpu": bt, "seq_len": t_len, "d_inner": d_total, "d_state": n, "chunk": kk,
-                   "parallelism": (f"d_inner-shard x{world} + NCCL all-reduce of packed [dB|dC] "
-                                   f"({2 * bt * t_len * n * 4} B)" if channel else
-                                   f"batch-shard x{world} (no collective)"),
-                   "l2": "inputs larger than L2 (%.0f MB touched per step)" % ((fwd_b + bwd_b) / 1e6)},
+        "config": workload_config(args.config, shape, world, channel, d),
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
-        "roofline": {"kernel": "mms_bwd (bwd_kernel_w8 + reduce_kernel)", "bound": "hbm",
-                     "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
-                     "frac": achieved / hbm_gbs, "traffic": traffic,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "algorithmic_bytes_per_launch": bwd_b},
-        "step_roofline": {"t_hbm_us": t_hbm * 1e6, "t_mufu_us": t_mufu * 1e6,
-                          "t_mufu_us_at_max_clock": t_mufu_max * 1e6,
-                          "t_step_us": t_step * 1e6,
-                          "frac": max(t_hbm, t_mufu) / t_step,
-                          "frac_at_max_clock": max(t_hbm, t_mufu_max) / t_step,
-                          "exps_per_step": exps, "bytes_per_step": fwd_b + bwd_b,
-                          "mufu_rate": f"{MUFU_EX2_PER_CLK_SM:.0f} ex2/clk/SM x {N_SM} SMs x "
-                                       f"{sm_mhz:.0f} MHz (median SM clock sampled under load)"},
+        "roofline": roof,
+        "step_roofline": step_roofline(t_step, fwd_b + bwd_b, 2 * bdn, hbm_gbs, ex2_per_s,
+                                       rates, sm_mhz, sm_max_default),
+        "pipe_rates": dict(rates, unit="operations per SM per clock (thread-level; FFMA2 as 2 FMAs)"),
         "clocks": clk,
         "gpu_launches": launches_per_step(bt, t_len, d, n, kk) * K,
     }
 
     if kk != 64 and not args.no_stride64:
-        line["reference_stride"] = time_stride(lib, _native, (bt, t_len, d, n, 64), device,
-                                               (x, dt, aneg, b_in, c_in, dy), stream)
+        s64 = time_stride(lib, _native, (bt, t_len, d, n, 64), device,
+                          (x, dt, aneg, b_in, c_in, dy), stream)
+        t64 = (s64["fwd_ms"] + s64["bwd_ms"]) * 1e-3
+        s64["step_roofline"] = step_roofline(t64, fwd_b + bwd_b, 2 * bdn, hbm_gbs, ex2_per_s,
+                                             rates, sm_mhz, sm_max_default)
+        s64["roofline"] = kernel_roofline("mms_bwd (bwd_kernel_cp + reduce_kernel)",
+                                          s64["bwd_ms"] * 1e-3, bwd_b, bdn, hbm_gbs, ex2_per_s,
+                                          BWD_FP32_LANES_PER_STATE_STEP * bdn, ffma_per_s)
+        s64["roofline"]["note"] = ("algorithmic units as at stride 8; at stride 64 the kernel "
+                                   "also recomputes each chunk's states once (2 exp2 per state-step)")
+        line["stride64"] = s64
     if kk == 8 and n in (12, 16) and d % 8 == 0 and world == 1 and not args.no_bf16:
         line["bf16"] = time_bf16(lib, _native, shape, device, (x, dt, aneg, b_in, c_in, dy),
                                  stream, hbm_gbs)
         if not args.no_e2e:
             line["bf16"]["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan,
                                           bf16=True)
+    del x, dt, aneg, b_in, c_in, dy, y, ckpt, dx, ddt, daneg, dbc, ws
+    torch.cuda.empty_cache()
+    # config 4 split over the N GPUs' channels, with its one collective
+    if not args.no_c4 and args.config != "c4":
+        line["c4_channel_shard"] = run_c4_channel(args, device, world, rank, ex2_per_s, hbm_gbs)
     # e2e through the public API from pinned host buffers
     if not args.no_e2e:
         line["e2e"] = run_e2e(args, shape, device, world, rank, selective_scan, channel)
@@ -425,6 +469,94 @@ def run_native(args, shape):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def step_roofline(t_step, nbytes, exps, hbm_gbs, ex2_per_s, rates, sm_mhz, sm_max_mhz):
+    """fwd + bwd against max(algorithmic HBM bytes / HBM bandwidth, exp2 count
+    (one per state-step each way) / measured MUFU rate)."""
+    t_hbm, t_mufu = nbytes / (hbm_gbs * 1e9), exps / ex2_per_s
+    t_mufu_max = t_mufu * sm_mhz / sm_max_mhz
+    return {"t_hbm_us": t_hbm * 1e6, "t_mufu_us": t_mufu * 1e6,
+            "t_mufu_us_at_max_clock": t_mufu_max * 1e6, "t_step_us": t_step * 1e6,
+            "bound": "mufu" if t_mufu >= t_hbm else "hbm",
+            "frac": max(t_hbm, t_mufu) / t_step,
+            "frac_at_max_clock": max(t_hbm, t_mufu_max) / t_step,
+            "exps_per_step": exps, "bytes_per_step": nbytes,
+            "mufu_rate": f"{rates['ex2']} ex2/clk/SM (measured in this run) x {N_SM} SMs x "
+                         f"{sm_mhz:.0f} MHz (median SM clock sampled under load)"}
+
+
+def run_c4_channel(args, device, world, rank, ex2_per_s, hbm_gbs, steps=20, warmup=3):
+    """Config 4 (B4 T4096 D8192 N16, K 8) with d_inner split over the ranks:
+    each rank scans its channels (B, C replicated) and the backward's packed
+    [dB|dC] partials (2*B*T*N floats) are summed by one NCCL all-reduce. Time
+    is the slowest rank's device time over `steps` fwd + bwd + all-reduce
+    steps; the all-reduce is also timed on its own (events around it)."""
+    from mamba_metal import _native
+    from mamba_metal.sharded import channel_shard
+    lib = _native.load()
+    bt, t_len, d_total, n, kk = CONFIGS["c4"]
+    sl = channel_shard(d_total, world, rank) if world > 1 else slice(0, d_total)
+    x, dt, aneg, b_in, c_in, dy = make_inputs(bt, t_len, d_total, n, 4000, device)
+    x, dt, dy = (t[:, :, sl].contiguous() for t in (x, dt, dy))
+    aneg = aneg[sl].contiguous()
+    d = x.shape[2]
+    y, ckpt = torch.empty_like(x), torch.empty(bt, -(-t_len // kk), d, n, device=device)
+    dx, ddt, daneg = torch.empty_like(x), torch.empty_like(x), torch.empty_like(aneg)
+    dbc = torch.empty(2, bt, t_len, n, device=device)
+    nb = _native.bwd_workspace_size(bt, t_len, d, n, kk)
+    ws = torch.empty(nb, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+    sp = stream.cuda_stream
+    P = lambda t: t.data_ptr()  # noqa: E731
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+
+    def step(e=None):
+        if e: e[0].record(stream)
+        rc = lib.mms_fwd(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(y), P(ckpt), bt, t_len, d, n,
+                         kk, sp)
+        assert rc == 0, _native.status_string(rc)
+        if e: e[1].record(stream)
+        rc = lib.mms_bwd(P(x), P(dt), P(aneg), P(b_in), P(c_in), P(dy), P(ckpt), P(dx), P(ddt),
+                         P(daneg), P(dbc[0]), P(dbc[1]), P(ws), nb, bt, t_len, d, n, kk, sp)
+        assert rc == 0, _native.status_string(rc)
+        if e: e[2].record(stream)
+        if world > 1:
+            dist.all_reduce(dbc, op=dist.ReduceOp.SUM)
+        if e: e[3].record(stream)
+
+    for _ in range(warmup):
+        step()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    s0.record(stream)
+    for i in range(steps):
+        step(ev[i])
+    s1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    t_ms = max_over_ranks(s0.elapsed_time(s1), world, device)
+    mean = lambda a, b: statistics.mean(e[a].elapsed_time(e[b]) for e in ev)  # noqa: E731
+    fwd_ms, bwd_ms, ar_ms = mean(0, 1), mean(1, 2), mean(2, 3)
+    ar_ms_max = max_over_ranks(ar_ms, world, device)
+    fwd_b, bwd_b = algorithmic_bytes(bt, t_len, d, n)
+    bdn = bt * t_len * d * n
+    local = (fwd_ms + bwd_ms) * 1e-3
+    return {"workload": f"c4: scan fwd+bwd B{bt} T{t_len} D{d_total} N{n} K{kk}, d_inner "
+                        f"sharded {d} per GPU over {world} GPU(s)",
+            "value": bt * t_len * d_total * steps / (t_ms * 1e-3), "unit": UNIT,
+            "ms_per_step": t_ms / steps, "scaling": "strong", "n_gpus": world,
+            "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "allreduce_ms": ar_ms, "allreduce_ms_max": ar_ms_max,
+            "allreduce_bytes": dbc.numel() * 4,
+            "allreduce_busbw_gbs": (2 * (world - 1) / world * dbc.numel() * 4 / (ar_ms * 1e-3) / 1e9
+                                    if world > 1 and ar_ms > 0 else None),
+            "shard_step_roofline_frac": max((fwd_b + bwd_b) / (hbm_gbs * 1e9), 2 * bdn / ex2_per_s)
+                                        / local,
+            "parallelism": (f"d_inner-shard x{world} + NCCL all-reduce of packed [dB|dC] "
+                            f"({dbc.numel() * 4} B)" if world > 1 else "one GPU, no collective"),
+            "steps": steps, "warmup": warmup,
+            "gpu_launches": launches_per_step(bt, t_len, d, n, kk) * steps}
 
 
 def time_stride(lib, _native, shape, device, ins, stream, k=20):
@@ -512,8 +644,41 @@ def time_bf16(lib, _native, shape, device, ins, stream, hbm_gbs, k=20):
             "note": "bf16 x, dt, y, dy, dx, ddt; fp32 arithmetic, Aneg, B, C, ckpt; kernels only"}
 
 
+def numa_local_cpus(device):
+    """CPUs of the NUMA node the GPU hangs off (sysfs), or None."""
+    try:
+        pr = torch.cuda.get_device_properties(device)
+        bus = f"{pr.pci_domain_id:04x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        text = Path(f"/sys/bus/pci/devices/{bus}/local_cpulist").read_text().strip()
+        cpus = set()
+        for part in text.split(","):
+            lo, _, hi = part.partition("-")
+            cpus.update(range(int(lo), int(hi or lo) + 1))
+        node = Path(f"/sys/bus/pci/devices/{bus}/numa_node").read_text().strip()
+        return cpus & os.sched_getaffinity(0) or None, node
+    except (OSError, ValueError, AttributeError):
+        return None, None
+
+
 def run_e2e(args, shape, device, world, rank, selective_scan, channel=False, bf16=False):
-    """bf16: x, dt, dy and y, dx, ddt cross PCIe as bf16 (selective_scan_bf16)."""
+    """bf16: x, dt, dy and y, dx, ddt cross PCIe as bf16 (selective_scan_bf16).
+
+    The pinned host buffers are allocated (and first touched) with this process
+    bound to the CPUs of the GPU's own NUMA node, so the copies do not cross
+    the socket interconnect; the binding is undone afterwards."""
+    cpus, node = numa_local_cpus(device)
+    saved = os.sched_getaffinity(0)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    try:
+        out = _run_e2e(args, shape, device, world, rank, selective_scan, channel, bf16)
+    finally:
+        os.sched_setaffinity(0, saved)
+    out["numa"] = {"node": node, "cpus_bound": len(cpus) if cpus else None}
+    return out
+
+
+def _run_e2e(args, shape, device, world, rank, selective_scan, channel, bf16):
     bt, t_len, d_total, n, kk = shape
     host = make_inputs(bt, t_len, d_total, n, 2000 + (0 if channel else rank), "cpu")
     cd = torch.bfloat16 if bf16 else torch.float32        # channel arrays' storage
@@ -545,15 +710,22 @@ def run_e2e(args, shape, device, world, rank, selective_scan, channel=False, bf1
     dev_in = [[torch.empty(t.shape, dtype=t.dtype, device=device) for t in host] for _ in range(2)]
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_free = [torch.cuda.Event() for _ in range(2)]
+    k = max(3, min(args.steps, 20))
+    cin = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(k)]
+    cout = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(k)]
     for ev in ev_free:
         ev.record(comp)
 
-    def step(i):
+    def step(i, timed=False):
         j = i % 2
         s_in.wait_event(ev_free[j])                  # the scan that last read buffer j is done
         with torch.cuda.stream(s_in):
+            if timed:
+                cin[i][0].record(s_in)
             for dst, src in zip(dev_in[j], host):
                 dst.copy_(src, non_blocking=True)
+            if timed:
+                cin[i][1].record(s_in)
             ev_in[j].record(s_in)
         comp.wait_event(ev_in[j])
         x, dt, aneg, b_in, c_in, dy = dev_in[j]
@@ -564,38 +736,56 @@ def run_e2e(args, shape, device, world, rank, selective_scan, channel=False, bf1
         outs = (y.detach(),) + tuple(grads)
         s_out.wait_stream(comp)
         with torch.cuda.stream(s_out):
+            if timed:
+                cout[i][0].record(s_out)
             for dst, src in zip(outs_h, outs):
                 dst.copy_(src, non_blocking=True)
                 src.record_stream(s_out)
+            if timed:
+                cout[i][1].record(s_out)
 
     for i in range(max(2, min(args.warmup, 5))):
         step(i)
     torch.cuda.synchronize()
-    k = max(3, min(args.steps, 20))
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
     s.record(comp)
     s_in.wait_event(s)
     for i in range(k):
-        step(i)
+        step(i, timed=True)
     comp.wait_stream(s_out)
     e.record(comp)
     torch.cuda.synchronize()
     t_ms = max_over_ranks(s.elapsed_time(e), world, device)
     total = bt * t_len * d_total if channel else world * bt * t_len * d
     api = ("mamba_metal.selective_scan_bf16" if bf16 else "mamba_metal.selective_scan(impl='cuda')")
+    t_in = statistics.mean(c[0].elapsed_time(c[1]) for c in cin) * 1e-3
+    t_out = statistics.mean(c[0].elapsed_time(c[1]) for c in cout) * 1e-3
     return {"value": total * k / (t_ms * 1e-3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": k,
+            "copy_gbs_per_rank": {"h2d": h2d / t_in / 1e9, "d2h": d2h / t_out / 1e9,
+                                  "note": "this rank's copy streams while they run (they overlap "
+                                          "the scan and, with N > 1, the other ranks' copies)"},
             "api": api + " + torch.autograd.grad, pinned host I/O; "
                    "copies in / out on their own streams, overlapping the previous and next step"}
 
 
 def run_train(args, device):
-    """Config 2: TinyMamba fp32 train step (fwd + bwd + AdamW), tokens/s."""
+    """Config 2: TinyMamba fp32 train step (fwd + bwd + AdamW), tokens/s and the
+    CUDA allocator's peak over a step (the reference bench's peak_gb,
+    bench/bench.py:115-121), at the package's checkpoint stride and at 64."""
+    out = _train(device, None)
+    out["stride64"] = _train(device, 64, timed_steps=3)
+    return out
+
+
+def _train(device, ssm_chunk, timed_steps=10):
     from mamba_metal import MambaConfig, TinyMamba
+    from mamba_metal.scan import SSM_CHUNK
+    ssm_chunk = ssm_chunk or SSM_CHUNK
     cfg = MambaConfig(vocab_size=32768, d_model=640, n_layers=12, d_ff=2560, max_seq_len=512,
-                      d_state=16, scan_impl="cuda")
+                      d_state=16, scan_impl="cuda", ssm_chunk=ssm_chunk)
     torch.manual_seed(0)
     model = TinyMamba(cfg).to(device)
     opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
@@ -612,7 +802,8 @@ def run_train(args, device):
     for _ in range(3):
         step()
     torch.cuda.synchronize()
-    k = 10
+    torch.cuda.reset_peak_memory_stats(device)
+    k = timed_steps
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(k):
@@ -620,8 +811,12 @@ def run_train(args, device):
     e.record()
     torch.cuda.synchronize()
     ms = s.elapsed_time(e) / k
+    peak = torch.cuda.max_memory_allocated(device) / 2**30
+    n_params, d_inner = model.count_params(), model.d_inner
+    del model, opt
+    torch.cuda.empty_cache()
     return {"tok_per_s": 16 * 512 / (ms * 1e-3), "ms_per_step": ms, "loss": float(loss.item()),
-            "params": model.count_params(), "d_inner": model.d_inner,
+            "peak_gb": peak, "ssm_chunk": ssm_chunk, "params": n_params, "d_inner": d_inner,
             "config": "TinyMamba vocab 32768, d_model 640, 12 layers, d_ff 2560, d_state 16, "
                       "batch 16 x seq 512, fp32, AdamW; scan on the CUDA kernels"}
 
@@ -787,8 +982,12 @@ def main():
     ap.add_argument("--impl", choices=("native", "reference"), default="native")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c1")
     ap.add_argument("--chunk", type=int, default=None, help="checkpoint stride (default: the config's, 8)")
-    ap.add_argument("--cpu-budget", type=float, default=18.0,
-                    help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of timed CPU work for the cpu_baseline (at least one full step)")
+    ap.add_argument("--ref-budget", type=float, default=120.0,
+                    help="--impl reference: seconds of timed CPU steps at most (at least one)")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="skip the config-4 channel-sharded timing (with its all-reduce)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

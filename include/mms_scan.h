@@ -30,7 +30,10 @@
  *     Bt, D >= 1, T >= 1. B, C, Aneg, ckpt, dB, dC, dAneg must be 16-byte
  *     aligned (row strides are then 16-byte multiples because N % 4 == 0);
  *     x, dt, y, dy, dx, ddt need 4-byte alignment.
- *   - Stateless and reentrant; calls on different streams may overlap.
+ *   - Stateless and reentrant, calls on different streams may overlap, with
+ *     two exceptions: mms_bwd_noalloc() shares one static scratch array
+ *     between all its calls (overlapping calls race), and the test hook
+ *     mms_debug_set_wait() changes a process-wide setting.
  */
 #ifndef MMS_SCAN_H
 #define MMS_SCAN_H
@@ -137,6 +140,10 @@ int mms_bwd_proj(const float *x, const float *dt_logit, const float *a_param,
  *    MMS_ERR_TOO_LARGE (nothing is launched).
  *  - The first call on a device looks the scratch address up (cudaGetSymbolAddress,
  *    with that device current); make that first call before any stream capture.
+ *    The address is kept for the life of the process and is valid while the
+ *    device's primary context lives: after cudaDeviceReset() (or anything
+ *    else that destroys that context) do not call mms_bwd_noalloc again in the
+ *    same process.
  *  - All calls share the one scratch array: calls that overlap on the GPU
  *    (other streams, unordered host threads) race and must be serialised.
  *    Nothing in it needs clearing between calls.

@@ -94,12 +94,12 @@ std::atomic<int> g_skip_item{-1};
 }  // namespace
 
 namespace mms {
-uint32_t bwd_wait_limit()
+uint32_t tma_wait_limit()
 {
     const uint32_t v = g_wait_limit.load(std::memory_order_relaxed);
     return v ? v : (1u << 22);
 }
-int bwd_debug_skip_item() { return g_skip_item.load(std::memory_order_relaxed); }
+int tma_skip_item() { return g_skip_item.load(std::memory_order_relaxed); }
 }  // namespace mms
 
 extern "C" {

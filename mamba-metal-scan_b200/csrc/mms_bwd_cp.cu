@@ -538,8 +538,8 @@ cudaError_t launch_cp(const BwdArgs &a, float *part_bc, float *part_a, const flo
     const size_t smem = CpSmem::bytes<E>(CP_MAXM);         // one opt-in size for every M
     cudaError_t e = smem_opt_in<bwd_kernel_cp<E, PROJ>>(smem);
     if (e != cudaSuccess) return e;
-    const uint32_t limit = bwd_wait_limit();
-    const int skip = bwd_debug_skip_item();
+    const uint32_t limit = tma_wait_limit();
+    const int skip = tma_skip_item();
     dim3 grid((a.D + CP_DPB - 1) / CP_DPB, a.Bt, sp.S);
     bwd_kernel_cp<E, PROJ><<<grid, CP_THREADS, CpSmem::bytes<E>(M), stream>>>(
         a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,

@@ -56,13 +56,13 @@ constexpr float W8_LN2 = 0.6931471805599453f;
 // read and cleared by mms_device_status().
 __device__ unsigned int g_w8_timeout;
 
-// Bounded wait for a stage's copies: after 2^22 polls (each may suspend
-// briefly in hardware) the thread records a timeout and goes on, so a lost
-// copy turns into an error status instead of a hung GPU.
-__device__ __forceinline__ void w8_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < (1u << 22); ++i)
-        if (mbar_try(bar, parity)) return;
-    atomicOr(&g_w8_timeout, 1u);
+// Bounded wait for a stage's copies: at most `limit` polls (each may suspend
+// briefly in hardware). A wait that runs out makes the CTA leave (see the
+// kernel), so a lost copy turns into an error status instead of a hung GPU.
+__device__ __forceinline__ bool w8_wait(uint32_t bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try(bar, parity)) return true;
+    return false;
 }
 // The six tensor maps of the TMA staging path.
 struct W8Maps {
@@ -320,7 +320,7 @@ bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
               E *__restrict__ ddt, float *__restrict__ part_bc,
               float *__restrict__ part_a, const float *__restrict__ seg_e,
               int T, int D, int N, int nblk, int cps, const __grid_constant__ W8Maps maps,
-              Proj pj_in)
+              Proj pj_in, uint32_t wait_limit, int skip_item)
 {
     // the prologue is compiled in only where it is used
     Proj pj = pj_in;
@@ -343,10 +343,16 @@ bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
     float *pbc = part_bc + ((size_t)L.b * nblk + blockIdx.x) * T * 2 * N;
 
     // inputs of chunk c and the checkpoint it starts from (zeros for c == 0)
+    const int sg = blockIdx.z, nsg = gridDim.z;
+    const int clo = sg * cps, chi = min((sg + 1) * cps, nchunk) - 1;
+    const int nch = chi - clo + 1;
+
+    // inputs of chunk c (item chi - c of this CTA) and the checkpoint it starts
+    // from (zeros for c == 0); the test hook withholds item skip_item
     auto stage = [&](int buf, int c) {
         float *st = nat + buf * W8Shape::STAGEF;
         if constexpr (TMA) {
-            if (tid == 0) {
+            if (tid == 0 && chi - c != skip_item) {
                 const uint32_t bar = bars + 8 * buf, dst = smem_u32(st);
                 using Q = W8Tile<E>;
                 mbar_expect(bar, Q::BYTES);
@@ -371,10 +377,6 @@ bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
         }
     };
 
-    const int sg = blockIdx.z, nsg = gridDim.z;
-    const int clo = sg * cps, chi = min((sg + 1) * cps, nchunk) - 1;
-    const int nch = chi - clo + 1;
-
     W8Adj A;
 #pragma unroll
     for (int p = 0; p < 4; ++p) A.gad[p] = A.anx[p] = A.dac[p] = f2(0.f, 0.f);
@@ -398,9 +400,21 @@ bwd_kernel_w8(const E *__restrict__ x, const E *__restrict__ dt,
 
     for (int it = 0; it < nch; ++it) {
         const int c = chi - it;
-        if constexpr (TMA) w8_wait(bars + 8 * (it % W8_NAT), (it / W8_NAT) & 1);
-        else cp_wait<1>();
-        __syncthreads();                                   // chunk c staged; chunk c+1 walked
+        if constexpr (TMA) {
+            const bool ok = w8_wait(bars + 8 * (it % W8_NAT), (it / W8_NAT) & 1, wait_limit);
+            if (__syncthreads_or(!ok)) {
+                // a stage never arrived: leave together, after the copies still in flight
+                if (tid == 0) {
+                    for (int k = it; k < min(it + 2, nch); ++k)
+                        if (k != skip_item) w8_wait(bars + 8 * (k % W8_NAT), (k / W8_NAT) & 1, wait_limit);
+                    atomicOr(&g_w8_timeout, 1u);
+                }
+                return;
+            }
+        } else {
+            cp_wait<1>();
+            __syncthreads();                               // chunk c staged; chunk c+1 walked
+        }
         if (it > 0) {                                      // dB|dC partial of chunk c+1
             const int t0p = (c + 1) * W8_CH, nvp = min(W8_CH, T - t0p);
             for (int p = tid; p < W8_CH * 32; p += W8_THREADS) {
@@ -502,7 +516,7 @@ cudaError_t launch_w8p(const BwdArgs &a, float *part_bc, float *part_a, const fl
     auto mE = [](float *p) { return reinterpret_cast<E *>(p); };
     bwd_kernel_w8<VEC, TMA, PROJ, E><<<grid, W8_THREADS, smem, stream>>>(
         cE(a.x), cE(a.dt), a.aneg, a.B, a.C, cE(a.dy), a.ckpt, mE(a.dx), mE(a.ddt), part_bc, part_a,
-        seg_e, a.T, a.D, a.N, nblk, sp.cps, maps, a.proj);
+        seg_e, a.T, a.D, a.N, nblk, sp.cps, maps, a.proj, tma_wait_limit(), tma_skip_item());
     return cudaGetLastError();
 }
 

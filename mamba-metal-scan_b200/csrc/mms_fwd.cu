@@ -207,6 +207,20 @@ constexpr int S16_DPB = 128;                                 // channels (= thre
 #define MMS_S16_UNROLL 4
 #endif
 constexpr int S16_UNROLL = MMS_S16_UNROLL;                   // steps unrolled in the tile loop
+
+// How many of the 8 state pairs of the whole-state forward take their decays
+// from the FMA-pipe polynomial (ex2_poly2) instead of MUFU ex2: one ex2 per
+// state and step is the kernel's MUFU load (16 per SM per clock, the binding
+// pipe), while its FP32 work is 4 lanes per state and step out of 128 per SM
+// per clock, so a share of the exponentials on the FMA pipe balances the two.
+#ifndef MMS_FWD_POLY_PAIRS
+#define MMS_FWD_POLY_PAIRS 1
+#endif
+// `pair` is a constant after the step loop's unrolling, so each pair is
+// compiled to one of the two paths.
+__device__ __forceinline__ float2 fwd_decay(int pair, float2 x) {
+    return pair < MMS_FWD_POLY_PAIRS ? ex2_poly2(x) : ex2x2(x);
+}
 constexpr int S16_TT = MMS_S16_TT;                           // steps per staged tile
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
@@ -244,10 +258,12 @@ struct FwdMaps {
 // Set when a wait on a forward TMA stage gave up; read by mms_device_status().
 __device__ unsigned int g_fwd_timeout;
 
-__device__ __forceinline__ void fwd_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < (1u << 22); ++i)
-        if (mbar_try(bar, parity)) return;
-    atomicOr(&g_fwd_timeout, 1u);
+// Bounded wait for a tile's copies (at most `limit` polls); a wait that runs
+// out makes the CTA leave (see the kernel) instead of hanging the GPU.
+__device__ __forceinline__ bool fwd_wait(uint32_t bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try(bar, parity)) return true;
+    return false;
 }
 
 // TMA: tiles arrive by TMA tile loads (one thread, 4 per tile) that complete
@@ -261,7 +277,8 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, E *__restrict__ y,
                float *__restrict__ ckpt, int T, int D, int N, int K, int L, int cps,
-               const __grid_constant__ FwdMaps maps, Proj pj_in)
+               const __grid_constant__ FwdMaps maps, Proj pj_in, uint32_t wait_limit,
+               int skip_item)
 {
     Proj pj = pj_in;                                       // the prologue only where used
     pj.on = PROJ;
@@ -361,7 +378,7 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     auto stage = [&](int buf, int kt) {
         float *tile = tiles + buf * TT * ROWF;
         if constexpr (TMA) {
-            if (tid == 0) {
+            if (tid == 0 && kt != skip_item) {             // the test hook withholds one tile
                 const uint32_t bar = bars + 8 * buf, dst = smem_u32(tile);
                 mbar_expect(bar, S16Tile<E>::BYTES);
                 tma3(dst, &maps.x, d0, tb + kt * TT, b, bar);
@@ -400,9 +417,24 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
             if (k > 0) fence_async_smem();                 // tile k-1's y / checkpoints
             if (tid == 0) bulk_wait_read<0>();             // tile k-2's copies have left set k&1
         }
-        if constexpr (TMA) fwd_wait(bars + 8 * (k % FWD_STAGES), (k / FWD_STAGES) & 1);
-        else cp_wait<FWD_STAGES - 2>();
-        __syncthreads();
+        if constexpr (TMA) {
+            const bool ok = fwd_wait(bars + 8 * (k % FWD_STAGES), (k / FWD_STAGES) & 1, wait_limit);
+            if (__syncthreads_or(!ok)) {
+                // a tile never arrived: leave together, after the loads still in
+                // flight and the bulk stores already issued
+                if (tid == 0) {
+                    for (int j = k; j < min(k + FWD_STAGES - 1, ntiles); ++j)
+                        if (j != skip_item)
+                            fwd_wait(bars + 8 * (j % FWD_STAGES), (j / FWD_STAGES) & 1, wait_limit);
+                    if constexpr (BULK) bulk_wait<0>();
+                    atomicOr(&g_fwd_timeout, 1u);
+                }
+                return;
+            }
+        } else {
+            cp_wait<FWD_STAGES - 2>();
+            __syncthreads();
+        }
         if constexpr (BULK) {
             if (k > 0 && tid == 0) send(k - 1, pnck, pck0, pck1);
         }
@@ -437,8 +469,9 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float4 Bv = bp[q], Cv = cp[q];
-                h[2 * q] = fma2(ex2x2(mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
-                h[2 * q + 1] = fma2(ex2x2(mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1], mul2(bx2, hi(Bv)));
+                h[2 * q] = fma2(fwd_decay(2 * q, mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
+                h[2 * q + 1] = fma2(fwd_decay(2 * q + 1, mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1],
+                                    mul2(bx2, hi(Bv)));
                 acc[(2 * q) % MMS_FWD_ACC] = fma2(lo(Cv), h[2 * q], acc[(2 * q) % MMS_FWD_ACC]);
                 acc[(2 * q + 1) % MMS_FWD_ACC] = fma2(hi(Cv), h[2 * q + 1], acc[(2 * q + 1) % MMS_FWD_ACC]);
             }
@@ -517,7 +550,7 @@ static cudaError_t launch_fwd_s16_q(const FwdArgs &a, const FwdMaps &maps, SegPl
     fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E><<<grid, S16_DPB, smem, stream>>>(
         reinterpret_cast<const E *>(a.x), reinterpret_cast<const E *>(a.dt), a.aneg, a.B, a.C,
         reinterpret_cast<E *>(a.y), a.ckpt, a.T, a.D, a.N, a.K, sp.cps * a.K, sp.cps, maps,
-        a.proj);
+        a.proj, tma_wait_limit(), tma_skip_item());
     return cudaGetLastError();
 }
 

@@ -97,8 +97,8 @@ inline bool cp_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K % 8
 // barrier before a kernel gives up (default 2^22), and a staged item whose
 // copies are withheld (-1: none). Both are test hooks set through
 // mms_debug_set_wait (mms_api.cu); launchers read them at launch.
-uint32_t bwd_wait_limit();
-int bwd_debug_skip_item();
+uint32_t tma_wait_limit();
+int tma_skip_item();
 
 inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
 {

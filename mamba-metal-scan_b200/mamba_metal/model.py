@@ -30,7 +30,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from mamba_metal.scan import (gated_output, selective_scan, selective_scan_proj,
+from mamba_metal.scan import (SSM_CHUNK, gated_output, selective_scan, selective_scan_proj,
                               selective_scan_step, selective_scan_step_ref)
 
 
@@ -45,6 +45,7 @@ class MambaConfig:
     d_conv: int = 4
     d_inner: Optional[int] = None
     scan_chunk: int = 0       # time slice of the parallel_scan fallback; 0 = one pass
+    ssm_chunk: int = SSM_CHUNK  # checkpoint stride of the CUDA scan (memory vs recompute)
     scan_impl: str = "auto"   # 'auto' | 'cuda' | 'metal' | 'torch'
     fuse_proj: bool = True    # CUDA scan computes dt and softplus(A) itself (selective_scan_proj)
     fuse_gate: bool = True    # (y + D_skip) * silu(z) as one CUDA kernel each way (gated_output)
@@ -159,6 +160,7 @@ class MambaBlock(nn.Module):
         dm, ds, kc = cfg.d_model, cfg.d_state, cfg.d_conv
         self.d_inner = d_inner
         self.scan_chunk = cfg.scan_chunk
+        self.ssm_chunk = cfg.ssm_chunk
         self.scan_impl = cfg.scan_impl
         self.fuse_proj = cfg.fuse_proj
         self.fuse_gate = cfg.fuse_gate
@@ -193,9 +195,9 @@ class MambaBlock(nn.Module):
             # dt and Aneg computed inside the kernels from dt_proj(x) and A
             return selective_scan_proj(x, self.dt_proj(x), self.A, self.B_proj(x), self.C_proj(x),
                                        self.dt_min, self.dt_max, impl=self.scan_impl,
-                                       return_state=return_state)
+                                       chunk=self.ssm_chunk, return_state=return_state)
         dt, B_t, C_t, Aneg = self._proj(x)
-        r = selective_scan(x, dt, Aneg, B_t, C_t, impl=self.scan_impl,
+        r = selective_scan(x, dt, Aneg, B_t, C_t, impl=self.scan_impl, chunk=self.ssm_chunk,
                            return_state=return_state)
         if r is not None:
             return r
