@@ -258,6 +258,14 @@ int mms_probe_pipe(int kind, int iters, int blocks, float *sink, long long *cycl
                    unsigned *sm, void *stream);
 long long mms_probe_ops_per_cta(int kind, int iters);
 
+/*
+ * y[i] = 2^x[i] for n floats (device pointers) by one of the library's exp2
+ * paths: kind 0 MUFU ex2.approx.ftz, 1 the FMA-pipe polynomial the forward
+ * uses for a share of its decays, 2 the same on packed pairs. For the
+ * accuracy tests of the polynomial. No counterpart in the reference.
+ */
+int mms_probe_exp2(const float *x, float *y, long long n, int kind, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

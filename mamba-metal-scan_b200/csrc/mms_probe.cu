@@ -92,8 +92,33 @@ probe_kernel(float *sink, long long *cycles, unsigned *sm, int iters)
     }
 }
 
+// y[i] = 2^x[i] by MUFU ex2.approx.ftz (kind 0), the FMA-pipe polynomial
+// (kind 1) or its packed-pair form (kind 2, pairs (x[2j], x[2j+1])).
+__global__ void exp2_kernel(const float *__restrict__ x, float *__restrict__ y, long long n, int kind)
+{
+    const long long i = 2 * ((long long)blockIdx.x * blockDim.x + threadIdx.x);
+    if (i >= n) return;
+    const float a = x[i], b = i + 1 < n ? x[i + 1] : 0.f;
+    float2 r;
+    if (kind == 0) r = f2(ex2_fresh(a), ex2_fresh(b));
+    else if (kind == 1) r = f2(ex2_poly(a), ex2_poly(b));
+    else r = ex2_poly2(f2(a, b));
+    y[i] = r.x;
+    if (i + 1 < n) y[i + 1] = r.y;
+}
+
 }  // namespace
 }  // namespace mms
+
+extern "C" int mms_probe_exp2(const float *x, float *y, long long n, int kind, void *stream)
+{
+    if (!x || !y || n < 0 || kind < 0 || kind > 2) return MMS_ERR_INVALID_ARG;
+    if (n == 0) return MMS_OK;
+    const long long threads = (n + 1) / 2;
+    mms::exp2_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        x, y, n, kind);
+    return cudaGetLastError() == cudaSuccess ? MMS_OK : MMS_ERR_CUDA;
+}
 
 extern "C" int mms_probe_pipe(int kind, int iters, int blocks, float *sink, long long *cycles,
                               unsigned *sm, void *stream)

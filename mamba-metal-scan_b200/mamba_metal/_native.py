@@ -50,6 +50,7 @@ SIGNATURES = {
     "mms_debug_set_wait": ([ctypes.c_uint, _I], _I),
     "mms_probe_pipe": ([_I] * 3 + [_P] * 4, _I),
     "mms_probe_ops_per_cta": ([_I] * 2, ctypes.c_longlong),
+    "mms_probe_exp2": ([_P, _P, ctypes.c_longlong, _I, _P], _I),
 }
 
 # mms_probe_pipe kinds
