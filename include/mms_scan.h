@@ -59,7 +59,7 @@ extern "C" {
                                       for the backward                                   */
 
 /* Version of the ABI in this header (major * 100 + minor). */
-#define MMS_ABI_VERSION 104
+#define MMS_ABI_VERSION 105
 int mms_abi_version(void);
 
 /* Human-readable text for an MMS_* status. Never NULL. */

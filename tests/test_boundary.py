@@ -37,7 +37,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _native.load()
-    assert lib.mms_abi_version() == 104
+    assert lib.mms_abi_version() == 105
     for rc in range(9):
         assert _native.status_string(rc) != "unknown status"
     assert _native.status_string(99) == "unknown status"
