@@ -71,10 +71,10 @@ CONFIGS = {
 }
 
 
-def _splits(bt, t_len, d, n, k, dpb, ctas_per_sm):
+def _splits(bt, t_len, d, n, k, dpb, ctas_per_sm, min_base=N_SM):
     """The library's time-segment rule (seg_plan / seg_plan_s16), restated."""
     base = bt * (-(-d // dpb))
-    if base >= N_SM:
+    if base >= min_base:
         return False
     nchunk = -(-t_len // k)
     want = (ctas_per_sm * N_SM) // base
@@ -89,7 +89,8 @@ def launches_per_step(bt, t_len, d, n, k):
     while g < (n + 3) // 4:
         g *= 2
     per_sm = 4 if (8 < n <= 16 and k == 8) else 2         # backward CTAs per SM
-    split_b = _splits(bt, t_len, d, n, k, 256 // g, per_sm)
+    # the 8-state backward also splits below half a wave
+    split_b = _splits(bt, t_len, d, n, k, 256 // g, per_sm, 2 * N_SM if per_sm == 4 else N_SM)
     split_g = _splits(bt, t_len, d, n, k, 256 // g, per_sm)  # the G-lane forward's plan
     if 8 < n <= 16 and bt * d >= N_SM * 128:
         split_f = False                                   # whole-state forward, no split

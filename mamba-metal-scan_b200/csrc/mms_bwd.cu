@@ -773,7 +773,7 @@ BwdWorkspace bwd_workspace_layout(int Bt, int T, int D, int N, int K)
     w.nblk = (D + dpb - 1) / dpb;
     const int kk = K < T ? K : T;
     w.nseg = (kk + SEG - 1) / SEG;
-    w.plan = seg_plan(Bt, T, D, N, K);
+    w.plan = seg_plan(Bt, T, D, N, K, true);
     const size_t planes = (size_t)Bt * w.plan.S * D * N * sizeof(float);
     size_t off = 0;
     w.part_bc = off;

@@ -221,6 +221,13 @@ constexpr int S16_UNROLL = MMS_S16_UNROLL;                   // steps unrolled i
 __device__ __forceinline__ float2 fwd_decay(int pair, float2 x) {
     return pair < MMS_FWD_POLY_PAIRS ? ex2_poly2(x) : ex2x2(x);
 }
+
+// The 16 decays 2^(dt * nan2) of one step.
+__device__ __forceinline__ void fwd_decays(float2 (&dA)[8], float dtv, const float2 (&nan2)[8]) {
+    const float2 dt2 = f2(dtv, dtv);
+#pragma unroll
+    for (int p = 0; p < 8; ++p) dA[p] = fwd_decay(p, mul2(dt2, nan2[p]));
+}
 constexpr int S16_TT = MMS_S16_TT;                           // steps per staged tile
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
 
@@ -458,10 +465,12 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
             const float xv = to_f(tx[j * XROW + tid]);
             float dtv = to_f(tdt[j * XROW + tid]);
             if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
+            float2 dAc[8];
+            fwd_decays(dAc, dtv, nan2);
             const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW);
             const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
             const float bx = dtv * xv;
-            const float2 dt2 = f2(dtv, dtv), bx2 = f2(bx, bx);
+            const float2 bx2 = f2(bx, bx);
             // y = sum_n C*h over MMS_FWD_ACC independent partial sums (shorter chains)
             float2 acc[MMS_FWD_ACC];
 #pragma unroll
@@ -469,9 +478,8 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 const float4 Bv = bp[q], Cv = cp[q];
-                h[2 * q] = fma2(fwd_decay(2 * q, mul2(dt2, nan2[2 * q])), h[2 * q], mul2(bx2, lo(Bv)));
-                h[2 * q + 1] = fma2(fwd_decay(2 * q + 1, mul2(dt2, nan2[2 * q + 1])), h[2 * q + 1],
-                                    mul2(bx2, hi(Bv)));
+                h[2 * q] = fma2(dAc[2 * q], h[2 * q], mul2(bx2, lo(Bv)));
+                h[2 * q + 1] = fma2(dAc[2 * q + 1], h[2 * q + 1], mul2(bx2, hi(Bv)));
                 acc[(2 * q) % MMS_FWD_ACC] = fma2(lo(Cv), h[2 * q], acc[(2 * q) % MMS_FWD_ACC]);
                 acc[(2 * q + 1) % MMS_FWD_ACC] = fma2(hi(Cv), h[2 * q + 1], acc[(2 * q + 1) % MMS_FWD_ACC]);
             }
@@ -642,7 +650,7 @@ static cudaError_t launch_fwd_gvp(const FwdArgs &a, cudaStream_t stream)
     using S = FwdShape<G>;
     cudaError_t e = smem_opt_in<fwd_kernel<G, VEC, PROJ, E>>(S::SMEM);
     if (e != cudaSuccess) return e;
-    const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K);
+    const SegPlan sp = seg_plan(a.Bt, a.T, a.D, a.N, a.K, false);
     const int nchunk = (a.T + a.K - 1) / a.K;
     const int L = sp.cps * a.K;
     if (sp.S > 1) {
@@ -685,7 +693,7 @@ static cudaError_t launch_fwd_bf16(const FwdArgs &a, cudaStream_t stream)
         return cudaErrorInvalidValue;
     if (groups_for(a.N) == 4 && a.K >= 8 &&
         ((long long)a.Bt * a.D >= S16_MIN_CHANNELS ||
-         (seg_plan_s16(a.Bt, a.T, a.D, a.K).S > 1 && seg_plan(a.Bt, a.T, a.D, a.N, a.K).S > 1))) {
+         (seg_plan_s16(a.Bt, a.T, a.D, a.K).S > 1 && seg_plan(a.Bt, a.T, a.D, a.N, a.K, false).S > 1))) {
         FwdMaps maps;
         memset(&maps, 0, sizeof(maps));
         if (!fwd_maps(a, &maps)) return cudaErrorInvalidValue;
@@ -714,7 +722,7 @@ cudaError_t launch_fwd(const FwdArgs &a, cudaStream_t stream)
     // segmented whole-state one (B4 T4096 D4096: 569 vs 615 us).
     if (groups_for(a.N) == 4 &&
         ((long long)a.Bt * a.D >= S16_MIN_CHANNELS ||
-         (seg_plan_s16(a.Bt, a.T, a.D, a.K).S > 1 && seg_plan(a.Bt, a.T, a.D, a.N, a.K).S > 1 &&
+         (seg_plan_s16(a.Bt, a.T, a.D, a.K).S > 1 && seg_plan(a.Bt, a.T, a.D, a.N, a.K, false).S > 1 &&
           a.K >= 8 && vec_ok(a.D, a.x, a.dt) && vec_ok(a.D, a.y, a.y))))
         return launch_fwd_s16(a, stream);
     switch (groups_for(a.N)) {

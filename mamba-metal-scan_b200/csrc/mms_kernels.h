@@ -82,6 +82,7 @@ inline int groups_for(int N)
 // P_s = prod over the segment of exp(-dt*Aneg) = exp(-Aneg * sum dt).
 // The forward and backward use the same plan (it depends on the shape only).
 constexpr int N_SM = 148;
+
 struct SegPlan {
     int S;      // segments (1: no split)
     int cps;    // checkpoint chunks per segment
@@ -100,19 +101,26 @@ inline bool cp_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K % 8
 uint32_t tma_wait_limit();
 int tma_skip_item();
 
-inline SegPlan seg_plan(int Bt, int T, int D, int N, int K)
+// `backward`: the plan of the backward, else of the G-lane forward. The two
+// may differ: a backward segment starts from the forward's checkpoint at its
+// first chunk, whatever segments the forward ran.
+inline SegPlan seg_plan(int Bt, int T, int D, int N, int K, bool backward)
 {
     const int dpb = 256 / groups_for(N);
     const long long base = (long long)Bt * ((D + dpb - 1) / dpb);
     const int nchunk = (T + K - 1) / K;
     SegPlan p{1, nchunk};
-    // Splitting costs a local pass over S-1 segments (about 40 % more work for
-    // a fwd+bwd step), which pays only below one CTA per SM.
-    if (base >= N_SM) return p;
     // Segments for one whole wave of the backward: the 8-state kernel runs 4
     // CTAs per SM, the channel-pair and 4-state kernels (and the G-lane
     // forward) 2. More segments than one wave holds only add local-pass work.
     const long long per_sm = w8_shape(N, K) ? 4 : 2;
+    // Splitting costs a local pass over S-1 segments (about 40 % more work for
+    // a fwd+bwd step), which pays only when the batch rows x channel blocks
+    // leave SMs idle: below one CTA per SM, and for the 8-state backward (4
+    // per SM) below half a wave (measured at B4 T4096 D4096: 1528 us split in
+    // two against 1735 us unsplit; the forward there loses by splitting).
+    const long long min_base = backward && per_sm == 4 ? 2 * N_SM : N_SM;
+    if (base >= min_base) return p;
     const long long want = (per_sm * N_SM) / base;
     long long cps = (nchunk + want - 1) / want;
     if (cps < 2) cps = 2;                           // the forward keeps P_s in chunk cps-2
