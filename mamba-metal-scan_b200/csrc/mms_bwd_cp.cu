@@ -96,7 +96,7 @@ struct CpSmem {
     static constexpr int SLOT = CP_THREADS * 8;             // one entry state per thread
     template <typename E>
     static size_t bytes(int m) {
-        return sizeof(float) * ((size_t)CP_NAT * CpTile<E>::F + 2 * CP_SUB * 64 + SD + (size_t)(m - 1) * SLOT) + 64;
+        return sizeof(float) * ((size_t)CP_NAT * CpTile<E>::F + 2 * CP_SUB * 128 + SD + (size_t)(m - 1) * SLOT) + 64;
     }
 };
 
@@ -121,14 +121,16 @@ __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16 *p) {
     return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
 }
 
-// Per-thread constants. The arithmetic is scalar: packed FFMA2 / FMUL2 add no
-// FP32 throughput on this GPU (measured 122.6 vs 123.8 lanes per clock per
-// SM) and their register-pair operands cost moves.
+// Per-thread constants. Every float2 of a thread pairs its two channels
+// (channel 0, channel 1) for one state, so the per-channel step inputs (dt,
+// x, dy and dt*x) are natural pairs loaded by one 8-byte read, and the packed
+// FFMA2 / FMUL2 instructions take two elements per issue; B and C, which are
+// per state, come pre-duplicated from shared memory.
 struct CpLane {
     int lane, q, tau, pr;
     int d0c;                      // channel 0 of the pair
     bool dv0, dv1;
-    float nan[4][2];              // -Aneg*log2(e) of state s(m), [m][channel]
+    float2 nan[4];                // -Aneg*log2(e) of state s(m), (channel 0, channel 1)
     __device__ CpLane(const float *aneg, int D, int N, bool proj) {
         const int tid = threadIdx.x;
         lane = tid & 31;
@@ -141,72 +143,81 @@ struct CpLane {
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
             const int s = state(m);
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                const bool ok = (c ? dv1 : dv0) && s < N;
-                float a = ok ? __ldg(aneg + (size_t)(d0c + c) * N + s) : 0.f;
-                if (proj) a = ok ? softplus(a) : 0.f;
-                nan[m][c] = -a * MMS_LOG2E;
+            float a0 = dv0 && s < N ? __ldg(aneg + (size_t)d0c * N + s) : 0.f;
+            float a1 = dv1 && s < N ? __ldg(aneg + (size_t)(d0c + 1) * N + s) : 0.f;
+            if (proj) {
+                a0 = dv0 && s < N ? softplus(a0) : 0.f;
+                a1 = dv1 && s < N ? softplus(a1) : 0.f;
             }
+            nan[m] = f2(-a0 * MMS_LOG2E, -a1 * MMS_LOG2E);
         }
     }
     __device__ int state(int m) const { return 4 * q + (m ^ tau); }
 };
 
-// One thread's 8 state values: [position m (state s(m))][channel].
+// One thread's 8 state values: [position m] = (channel 0, channel 1) of state s(m).
 struct St8 {
-    float v[4][2];
+    float2 v[4];
 };
 
-// B and C rows of the 8 steps in the four lane state orders,
-// [a (B, C)][t][tau][16]: (B_s(0), .., B_s(3)) of lane (q, tau) at [..][tau][4q].
-constexpr int CP_PERM = 2 * CP_SUB * 4 * 16;
+// B and C of the 8 steps duplicated per state, in the four lane state
+// orders: [a (B, C)][t][half][tau][q][4] holds (B_s(2h), B_s(2h), B_s(2h+1),
+// B_s(2h+1)) of lane (q, tau) at half h; a warp's 16-byte reads of one half
+// touch 16 consecutive 16-byte pieces (no bank conflicts).
+constexpr int CP_DUP_STEP = 2 * 4 * 4 * 4;              // floats per step and array
+constexpr int CP_DUP = 2 * CP_SUB * CP_DUP_STEP;        // both arrays, 2048 floats
 
 template <typename E>
 struct CpView {
     const E *x, *dt, *dy;        // channel pair of this lane, step stride CP_DPB
-    const float *B, *C;          // this lane's permuted rows, step stride 64
+    const float *B, *C;          // this lane's duplicated rows, step stride CP_DUP_STEP
     const float *ck;             // entry slab [64][16]
-    __device__ CpView(const float *st, const float *perm, const CpLane &L) {
+    __device__ CpView(const float *st, const float *dup, const CpLane &L) {
         x = reinterpret_cast<const E *>(st) + 2 * L.pr;
         dt = reinterpret_cast<const E *>(st + CpTile<E>::ARR) + 2 * L.pr;
         dy = reinterpret_cast<const E *>(st + 2 * CpTile<E>::ARR) + 2 * L.pr;
-        B = perm + L.tau * 16 + 4 * L.q;
-        C = B + CP_SUB * 64;
+        B = dup + L.tau * 16 + 4 * L.q;
+        C = B + CP_SUB * CP_DUP_STEP;
         ck = st + CpTile<E>::CK;
     }
     __device__ float2 xs(int t) const { return ld_pair(x + t * CP_DPB); }
     __device__ float2 dts(int t) const { return ld_pair(dt + t * CP_DPB); }
     __device__ float2 dys(int t) const { return ld_pair(dy + t * CP_DPB); }
-    __device__ float4 Bs(int t) const { return *reinterpret_cast<const float4 *>(B + t * 64); }
-    __device__ float4 Cs(int t) const { return *reinterpret_cast<const float4 *>(C + t * 64); }
+    // (B_s(2h), B_s(2h), B_s(2h+1), B_s(2h+1))
+    __device__ float4 Bs(int t, int h) const { return *reinterpret_cast<const float4 *>(B + t * CP_DUP_STEP + h * 64); }
+    __device__ float4 Cs(int t, int h) const { return *reinterpret_cast<const float4 *>(C + t * CP_DUP_STEP + h * 64); }
     // the chunk's entry state from the checkpoint slab
     __device__ void entry(St8 &h, const CpLane &L) const {
         const float *r0 = ck + (2 * L.pr) * 16, *r1 = r0 + 16;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            h.v[m][0] = r0[L.state(m)];
-            h.v[m][1] = r1[L.state(m)];
-        }
+        for (int m = 0; m < 4; ++m) h.v[m] = f2(r0[L.state(m)], r1[L.state(m)]);
     }
 };
 
-__device__ __forceinline__ float cpt(const float2 &v, int c) { return c ? v.y : v.x; }
+__device__ __forceinline__ float2 dup_of(const float4 &lo4, const float4 &hi4, int m) {
+    return m == 0 ? lo(lo4) : m == 1 ? hi(lo4) : m == 2 ? lo(hi4) : hi(hi4);
+}
 
 // h <- one step; the step's dA returned in dA.
 template <typename E>
 __device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E> &v, const CpLane &L, int t) {
-    const float2 dt2 = v.dts(t), x2 = v.xs(t);
-    const float4 Bv = v.Bs(t);
+    const float2 dt2 = v.dts(t);
+    const float2 bx2 = mul2(dt2, v.xs(t));
+    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        const float dtc = cpt(dt2, c), bx = dtc * cpt(x2, c);
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            dA.v[m][c] = ex2(dtc * L.nan[m][c]);
-            h.v[m][c] = fmaf(dA.v[m][c], h.v[m][c], bx * comp(Bv, m));
-        }
+    for (int m = 0; m < 4; ++m) {
+        dA.v[m] = ex2x2(mul2(dt2, L.nan[m]));
+        h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, dup_of(B0, B1, m)));
     }
+}
+
+// h <- one step with a known dA (no ex2).
+template <typename E>
+__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E> &v, int t) {
+    const float2 bx2 = mul2(v.dts(t), v.xs(t));
+    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, dup_of(B0, B1, m)));
 }
 
 // One backward step t: hc = h_t, hp = h_{t-1}, dA = dA_t; r carries
@@ -218,31 +229,28 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
                                              const Proj &pj)
 {
     const float2 dt2 = v.dts(t), x2 = v.xs(t), dy2 = v.dys(t);
-    const float4 Bv = v.Bs(t), Cv = v.Cs(t);
-    float sB[2], sA[2], vb[4], vc[4];
+    const float2 bx2 = mul2(dt2, x2);
+    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1), C0 = v.Cs(t, 0), C1 = v.Cs(t, 1);
+    float2 sB, sA, P[4];                  // P[m] = (sum over the pair of g*dt*x, of dy*h_t)
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        const float dtc = cpt(dt2, c), dyc = cpt(dy2, c), bx = dtc * cpt(x2, c);
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const float g = fmaf(dyc, comp(Cv, m), r.v[m][c]);
-            const float rn = dA.v[m][c] * g;
-            const float u = rn * hp.v[m][c];
-            sB[c] = m ? fmaf(g, comp(Bv, m), sB[c]) : g * comp(Bv, m);
-            sA[c] = m ? fmaf(L.nan[m][c], u, sA[c]) : L.nan[m][c] * u;
-            dac.v[m][c] = fmaf(dtc, u, dac.v[m][c]);
-            vb[m] = c ? fmaf(bx, g, vb[m]) : bx * g;
-            vc[m] = c ? fmaf(dyc, hc.v[m][c], vc[m]) : dyc * hc.v[m][c];
-            r.v[m][c] = rn;
-        }
+    for (int m = 0; m < 4; ++m) {
+        const float2 g = fma2(dy2, dup_of(C0, C1, m), r.v[m]);
+        const float2 rn = mul2(dA.v[m], g);
+        const float2 u = mul2(rn, hp.v[m]);
+        sB = m ? fma2(g, dup_of(B0, B1, m), sB) : mul2(g, dup_of(B0, B1, m));
+        sA = m ? fma2(L.nan[m], u, sA) : mul2(L.nan[m], u);
+        dac.v[m] = fma2(dt2, u, dac.v[m]);
+        const float2 pb = mul2(g, bx2), pc = mul2(dy2, hc.v[m]);
+        P[m] = f2(pb.x + pb.y, pc.x + pc.y);
+        r.v[m] = rn;
     }
     {   // dx = dt*sum gB, ddt = x*sum gB + ln2*sum nan*u, over the pair's 4 state lanes
-        const float dx0 = dt2.x * sB[0], dx1 = dt2.y * sB[1];
-        const float dd0 = fmaf(x2.x, sB[0], CP_LN2 * sA[0]), dd1 = fmaf(x2.y, sB[1], CP_LN2 * sA[1]);
+        const float2 pdx = mul2(dt2, sB);
+        const float2 pddt = fma2(x2, sB, mul2(f2(CP_LN2, CP_LN2), sA));
         const bool b0 = L.lane & 1, b1 = (L.lane >> 1) & 1;
-        float kx = b0 ? dx1 : dx0, kd = b0 ? dd1 : dd0;
-        kx += __shfl_xor_sync(0xffffffffu, b0 ? dx0 : dx1, 1);
-        kd += __shfl_xor_sync(0xffffffffu, b0 ? dd0 : dd1, 1);
+        float kx = b0 ? pdx.y : pdx.x, kd = b0 ? pddt.y : pddt.x;
+        kx += __shfl_xor_sync(0xffffffffu, b0 ? pdx.x : pdx.y, 1);
+        kd += __shfl_xor_sync(0xffffffffu, b0 ? pddt.x : pddt.y, 1);
         float kv = b1 ? kd : kx;
         kv += __shfl_xor_sync(0xffffffffu, b1 ? kx : kd, 2);
         // this lane ends with channel b0, kind b1 (0 dx, 1 ddt); outp points at
@@ -254,15 +262,12 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
         if (t < nv && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
     }
     // dB | dC over the warp's 8 channel pairs: lane bits 4, 3 select-free, bit 2 by kind
-    vb[0] += __shfl_xor_sync(0xffffffffu, vb[2], 16);
-    vb[1] += __shfl_xor_sync(0xffffffffu, vb[3], 16);
-    vc[0] += __shfl_xor_sync(0xffffffffu, vc[2], 16);
-    vc[1] += __shfl_xor_sync(0xffffffffu, vc[3], 16);
-    vb[0] += __shfl_xor_sync(0xffffffffu, vb[1], 8);
-    vc[0] += __shfl_xor_sync(0xffffffffu, vc[1], 8);
+    P[0] = add2(P[0], shfl2(P[2], 16));
+    P[1] = add2(P[1], shfl2(P[3], 16));
+    P[0] = add2(P[0], shfl2(P[1], 8));
     const int kb = (L.lane >> 2) & 1;
-    float kk = kb ? vc[0] : vb[0];
-    kk += __shfl_xor_sync(0xffffffffu, kb ? vb[0] : vc[0], 4);
+    float kk = kb ? P[0].y : P[0].x;
+    kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 4);
     sd[(t * CP_WARPS + warp) * 32 + kb * 16 + L.state(0)] = kk;
 }
 
@@ -277,21 +282,10 @@ __device__ __forceinline__ void cp_entry(St8 &h, const CpView<E> &v, const CpLan
     } else {
         const float4 a0 = reinterpret_cast<const float4 *>(slot_in)[0];
         const float4 a1 = reinterpret_cast<const float4 *>(slot_in)[1];
-        h.v[0][0] = a0.x; h.v[0][1] = a0.y; h.v[1][0] = a0.z; h.v[1][1] = a0.w;
-        h.v[2][0] = a1.x; h.v[2][1] = a1.y; h.v[3][0] = a1.z; h.v[3][1] = a1.w;
-    }
-}
-
-// h <- one step with a known dA (no ex2).
-template <typename E>
-__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E> &v, int t) {
-    const float2 dt2 = v.dts(t), x2 = v.xs(t);
-    const float4 Bv = v.Bs(t);
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-        const float bx = cpt(dt2, c) * cpt(x2, c);
-#pragma unroll
-        for (int m = 0; m < 4; ++m) h.v[m][c] = fmaf(dA.v[m][c], h.v[m][c], bx * comp(Bv, m));
+        h.v[0] = lo(a0);
+        h.v[1] = hi(a0);
+        h.v[2] = lo(a1);
+        h.v[3] = hi(a1);
     }
 }
 
@@ -331,31 +325,22 @@ __device__ __forceinline__ void cp_walk(const CpView<E> &v, const CpLane &L, int
 }
 
 // The item sequence of one CTA: chunks chi down to clo; in a chunk with mv
-// valid sub-chunks, a pre-pass over sub-chunks 0..mv-2, then walks of mv-1..0.
-struct CpItems {
-    int chi, M, mv_first, first_items, per_chunk, total;
-    __device__ CpItems(int clo, int chi_, int M_, int T, int K, int nchunk) : chi(chi_), M(M_) {
-        const int steps_last = T - chi * K;                       // valid steps of chunk chi
-        mv_first = chi == nchunk - 1 ? min(M, (steps_last + CP_SUB - 1) / CP_SUB) : M;
-        first_items = 2 * mv_first - 1;
-        per_chunk = 2 * M - 1;
-        total = first_items + (chi - clo) * per_chunk;
+// valid sub-chunks, a pre-pass over sub-chunks 0..mv-2, then walks of
+// mv-1..0 (2*mv - 1 items). A cursor steps through it without divisions.
+struct CpCursor {
+    int c, k, mvc;              // chunk, item within the chunk, its valid sub-chunks
+    int M;
+    __device__ CpCursor(int chi, int M_, int T, int K, int nchunk) : c(chi), k(0), M(M_) {
+        mvc = chi == nchunk - 1 ? min(M, (T - chi * K + CP_SUB - 1) / CP_SUB) : M;
     }
-    // item i -> chunk, sub-chunk within it, walk?
-    __device__ void at(int i, int &c, int &j, bool &walk) const {
-        int mvc, k;
-        if (i < first_items) {
-            c = chi;
-            k = i;
-            mvc = mv_first;
-        } else {
-            const int e = i - first_items;
-            c = chi - 1 - e / per_chunk;
-            k = e % per_chunk;
+    __device__ bool walk() const { return k >= mvc - 1; }
+    __device__ int j() const { return k >= mvc - 1 ? 2 * mvc - 2 - k : k; }
+    __device__ void next() {
+        if (++k == 2 * mvc - 1) {
+            --c;
+            k = 0;
             mvc = M;
         }
-        walk = k >= mvc - 1;
-        j = walk ? 2 * mvc - 2 - k : k;
     }
 };
 
@@ -371,8 +356,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     using Q = CpTile<E>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;                                  // [CP_NAT][Q::F]
-    float *perm = stages + CP_NAT * Q::F;                  // B, C in the lane orders (CP_PERM)
-    float *sd = perm + CP_PERM;                            // [8][4][32]
+    float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (CP_DUP)
+    float *sd = dup + CP_DUP;                              // [8][4][32]
     float *slots = sd + CpSmem::SD;                        // [M-1][128][8]
     const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * CpSmem::SLOT);
 
@@ -387,98 +372,113 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 
     const int sg = blockIdx.z, nsg = gridDim.z;
     const int clo = sg * cps, chi = min((sg + 1) * cps, nchunk) - 1;
-    const CpItems items(clo, chi, M, T, K, nchunk);
+    const int first_items = 2 * CpCursor(chi, M, T, K, nchunk).mvc - 1;
+    const int total = first_items + (chi - clo) * (2 * M - 1);
 
-    auto issue = [&](int i) {                              // thread 0: TMA loads of item i
-        if (i >= items.total || i == skip_item) return;
-        int c, j;
-        bool walk;
-        items.at(i, c, j, walk);
-        const int buf = i % CP_NAT;
+    // thread 0: TMA loads of the item at cursor `at`, number i, into stage i % 3
+    auto issue = [&](const CpCursor &at, int i, int buf) {
+        if (i == skip_item) return;
         const uint32_t bar = bars + 8 * buf, dst = smem_u32(stages + buf * Q::F);
-        const int t0 = (c * M + j) * CP_SUB;
+        const int t0 = (at.c * M + at.j()) * CP_SUB;
         mbar_expect(bar, Q::BYTES);
         tma3(dst, &maps.x, d0, t0, brow, bar);
         tma3(dst + 4 * Q::ARR, &maps.dt, d0, t0, brow, bar);
         tma3(dst + 8 * Q::ARR, &maps.dy, d0, t0, brow, bar);
         tma3(dst + 4 * Q::BC, &maps.B, 0, t0, brow, bar);
         tma3(dst + 4 * (Q::BC + CP_SUB * 16), &maps.C, 0, t0, brow, bar);
-        tma4(dst + 4 * Q::CK, &maps.ck, 0, d0, c - 1, brow, bar);
+        tma4(dst + 4 * Q::CK, &maps.ck, 0, d0, at.c - 1, brow, bar);
     };
 
     St8 r, dac;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) r.v[m][0] = r.v[m][1] = dac.v[m][0] = dac.v[m][1] = 0.f;
+    for (int m = 0; m < 4; ++m) r.v[m] = dac.v[m] = f2(0.f, 0.f);
     if (sg + 1 < nsg) {                                    // adjoint carry from the later segments
         const float *src = seg_e + ((size_t)brow * nsg + sg) * plane + (size_t)L.d0c * N;
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
             const int s = L.state(m);
-            r.v[m][0] = L.dv0 && s < N ? src[s] : 0.f;
-            r.v[m][1] = L.dv1 && s < N ? src[N + s] : 0.f;
+            r.v[m] = f2(L.dv0 && s < N ? src[s] : 0.f, L.dv1 && s < N ? src[N + s] : 0.f);
         }
     }
 
+    CpCursor ahead(chi, M, T, K, nchunk);                  // thread 0: the next item to issue
     if (tid == 0) {
         for (int s = 0; s < CP_NAT; ++s) mbar_init(bars + 8 * s, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        issue(0);
-        issue(1);
+        for (int i = 0; i < 2 && i < total; ++i) {
+            issue(ahead, i, i);
+            ahead.next();
+        }
     }
     __syncthreads();
 
-    // dB|dC partial of the walked sub-chunk starting at step t0p (nvp steps)
+    // this thread's share of the dB|dC flush: rows fr and fr + 4 of a walked
+    // sub-chunk, column fj of the four warps' sums
+    const int fr = tid >> 5, fj = tid & 31;
+    const bool fvalid = (fj & 15) < N;
+    float *pbc_col = pbc + (fj >> 4) * N + (fj & 15);
     auto flush = [&](int t0p, int nvp) {
-        for (int p = tid; p < CP_SUB * 32; p += CP_THREADS) {
-            const int i = p >> 5, j = p & 31;
-            const int kind = j >> 4, n = j & 15;
-            if (i < nvp && n < N) {
-                const float *s = sd + i * CP_WARPS * 32 + j;
-                pbc[(size_t)(t0p + i) * 2 * N + kind * N + n] = (s[0] + s[32]) + (s[64] + s[96]);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int i = fr + 4 * h;
+            if (i < nvp && fvalid) {
+                const float *q = sd + i * CP_WARPS * 32 + fj;
+                pbc_col[(size_t)(t0p + i) * 2 * N] = (q[0] + q[32]) + (q[64] + q[96]);
             }
         }
     };
+    // this thread's share of the B, C duplication: lane order pta, quad pq,
+    // half ph, steps pt and pt + 4
+    const int pq = tid & 3, pta = (tid >> 2) & 3, ph = (tid >> 4) & 1, pt = tid >> 5;
+    const int ps0 = 4 * pq + ((2 * ph) ^ pta), ps1 = 4 * pq + ((2 * ph + 1) ^ pta);
+    const int pdst = ((ph * 4 + pta) * 4 + pq) * 4;
 
+    CpCursor cur(chi, M, T, K, nchunk);
     int pend_t0 = -1, pend_nv = 0;
-    for (int i = 0; i < items.total; ++i) {
-        const int buf = i % CP_NAT;
-        const bool ok = cp_wait_bar(bars + 8 * buf, (i / CP_NAT) & 1, wait_limit);
+    int buf = 0;
+    uint32_t parity = 0;
+    for (int i = 0; i < total; ++i) {
+        const bool ok = cp_wait_bar(bars + 8 * buf, parity, wait_limit);
         if (__syncthreads_or(!ok)) {
             // a stage never arrived: leave together, after the copies still in flight
             if (tid == 0) {
-                for (int k = i; k < min(i + CP_NAT - 1, items.total); ++k)
+                for (int k = i; k < min(i + CP_NAT - 1, total); ++k)
                     if (k != skip_item) cp_wait_bar(bars + 8 * (k % CP_NAT), (k / CP_NAT) & 1, wait_limit);
                 atomicOr(&g_cp_timeout, 1u);
             }
             return;
         }
-        int c, j;
-        bool walk;
-        items.at(i, c, j, walk);
+        const int c = cur.c, j = cur.j();
+        const bool walk = cur.walk();
         float *st = stages + buf * Q::F;
         if (pend_t0 >= 0) {
             flush(pend_t0, pend_nv);
             pend_t0 = -1;
         }
-        // B, C of the 8 steps in the four lane state orders: perm[a][t][tau][16]
-        for (int e = tid; e < 2 * CP_SUB * 4 * 4; e += CP_THREADS) {
-            const int qq = e & 3, ta = (e >> 2) & 3, t = (e >> 4) & 7, a = e >> 7;
-            const float *src = st + Q::BC + (a * CP_SUB + t) * 16 + 4 * qq;
-            *reinterpret_cast<float4 *>(perm + ((a * CP_SUB + t) * 4 + ta) * 16 + 4 * qq) =
-                make_float4(src[0 ^ ta], src[1 ^ ta], src[2 ^ ta], src[3 ^ ta]);
-        }
+        // B, C of the 8 steps duplicated per state in the four lane orders
+#pragma unroll
+        for (int a = 0; a < 2; ++a)
+#pragma unroll
+            for (int tt = 0; tt < 2; ++tt) {
+                const int t = pt + 4 * tt;
+                const float *src = st + Q::BC + (a * CP_SUB + t) * 16;
+                const float b0 = src[ps0], b1 = src[ps1];
+                *reinterpret_cast<float4 *>(dup + (a * CP_SUB + t) * CP_DUP_STEP + pdst) =
+                    make_float4(b0, b0, b1, b1);
+            }
         if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
             float *dts = st + Q::ARR;
             for (int e = tid; e < CP_SUB * CP_DPB; e += CP_THREADS)
                 dts[e] = fmaf(pj.range, sigmoid_fast(dts[e]), pj.lo);
         }
-        if (tid == 0 && i + 2 < items.total) {
+        if (tid == 0 && i + 2 < total) {
             fence_async_smem();                            // stage (i+2)%3 was read before the barrier
-            issue(i + 2);
+            issue(ahead, i + 2, buf == 0 ? 2 : buf - 1);
+            ahead.next();
         }
         __syncthreads();
 
-        const CpView<E> v(st, perm, L);
+        const CpView<E> v(st, dup, L);
         const int u = c * M + j;                           // sub-chunk index in the sequence
         const int t0 = u * CP_SUB;
         const int nv = min(CP_SUB, T - t0);
@@ -490,14 +490,19 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 #pragma unroll
             for (int t = 0; t < CP_SUB; ++t) cp_advance<E>(h, dA, v, L, t);
             float4 *sl = reinterpret_cast<float4 *>(slots + (size_t)j * CpSmem::SLOT + tid * 8);
-            sl[0] = make_float4(h.v[0][0], h.v[0][1], h.v[1][0], h.v[1][1]);
-            sl[1] = make_float4(h.v[2][0], h.v[2][1], h.v[3][0], h.v[3][1]);
+            sl[0] = make_float4(h.v[0].x, h.v[0].y, h.v[1].x, h.v[1].y);
+            sl[1] = make_float4(h.v[2].x, h.v[2].y, h.v[3].x, h.v[3].y);
         } else {
             // this lane's output after the dx / ddt exchange: array (lane bit 1), channel (bit 0)
             E *outp = ((L.lane >> 1) & 1 ? ddt : dx) + rowD + (size_t)t0 * D + L.d0c + (L.lane & 1);
             cp_walk<E, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
             pend_t0 = t0;
             pend_nv = nv;
+        }
+        cur.next();
+        if (++buf == CP_NAT) {
+            buf = 0;
+            parity ^= 1u;
         }
     }
     __syncthreads();
@@ -507,8 +512,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     for (int m = 0; m < 4; ++m) {
         const int s = L.state(m);
         if (s < N) {
-            if (L.dv0) pa[s] = -dac.v[m][0];
-            if (L.dv1) pa[N + s] = -dac.v[m][1];
+            if (L.dv0) pa[s] = -dac.v[m].x;
+            if (L.dv1) pa[N + s] = -dac.v[m].y;
         }
     }
 }
