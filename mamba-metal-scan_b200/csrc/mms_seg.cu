@@ -30,6 +30,14 @@
 
 namespace mms {
 
+// The local pass is bound by MUFU: one ex2 per state-step against 3 FP32
+// lanes. MMS_SEGL_POLY moves a share of its exponentials to the FMA-pipe
+// polynomial (ex2_poly2): 0 none, 1 the first state pair on every other step
+// (25 %), 2 the first state pair on every step (50 %).
+#ifndef MMS_SEGL_POLY
+#define MMS_SEGL_POLY 1
+#endif
+
 constexpr int SEGL_THREADS = 256;
 constexpr int SEGL_STAGES = 3;
 constexpr int SEGL_TT = 16;
@@ -119,7 +127,10 @@ seg_local_kernel(const E *__restrict__ u, const E *__restrict__ dt,
             if (pj.on) dtv = tk + j < te ? fmaf(pj.range, sigmoid_fast(dtv), pj.lo) : 0.f;
             const float4 R = *reinterpret_cast<const float4 *>(r + CHF + 4 * g);
             const float2 dt2 = f2(dtv, dtv);
-            const float2 a0 = ex2x2(mul2(dt2, nan2[0])), a1 = ex2x2(mul2(dt2, nan2[1]));
+            // a share of the exponentials on the FMA pipe (see MMS_SEGL_POLY)
+            const bool poly0 = MMS_SEGL_POLY >= 2 || (MMS_SEGL_POLY == 1 && (jj & 1) == 0);
+            const float2 a0 = poly0 ? ex2_poly2(mul2(dt2, nan2[0])) : ex2x2(mul2(dt2, nan2[0]));
+            const float2 a1 = ex2x2(mul2(dt2, nan2[1]));
             sdt += dtv;
             if constexpr (!BWD) {
                 const float bx = dtv * uv;
