@@ -814,7 +814,7 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
-    if (G == 4 && MMS_BWD_CP && bwd_cp_applies(a)) {
+    if (G >= 4 && MMS_BWD_CP && bwd_cp_applies(a)) {
         e = launch_bwd_cp(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (G == 4 && bwd_w8_applies(a.N, a.K) && (MMS_BWD_W8 || a.bf16)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);

@@ -1,4 +1,4 @@
-// Backward selective scan on channel pairs (8 < N <= 16, checkpoint stride K =
+// Backward selective scan on channel pairs (8 < N <= 64, checkpoint stride K =
 // 8m with 1 <= m <= 8).
 //
 // Same mathematics as mms_bwd.cu (reference mamba_metal/scan.py:26-34, kernel
@@ -19,13 +19,16 @@
 //     instead of 2 with one channel per thread.
 //   * The 8 decays of a sub-chunk stay in registers from the rebuild to the
 //     walk, so every state-step costs one MUFU ex2 (at K = 8).
-// Lane layout: q = lane bits 0-1 picks states 4q..4q+3, lane bits 2-4 the
-// channel pair within the warp. The thread keeps its states in the order
-// 4q + (m XOR tau), tau = lane bits 4,3, so the first two butterfly levels of
-// the dB|dC reduction (over lane bits 4 and 3) are select-free; B and C are
-// rewritten once per sub-chunk into the four orders in shared memory.
+// Lane layout: NQ = N/4 (rounded up to 4, 8 or 16) lanes share a channel
+// pair; q = the low log2(NQ) lane bits picks states 4q..4q+3, the higher
+// lane bits the channel pair within the warp. The thread keeps its states in
+// the order 4q + (m XOR tau), tau = lane bits 4,3 (bit 4 only for NQ = 16),
+// so the butterfly levels of the dB|dC reduction over the pair bits among
+// lane bits 4 and 3 are select-free; B and C are rewritten once per
+// sub-chunk into the lane orders in shared memory. The dB|dC reduction has
+// log2(32/NQ) levels (3, 2, 1) and dx / ddt log2(NQ) (2, 3, 4).
 //
-// Time: a CTA (128 threads, 64 channels of one batch row, 3 per SM) walks its
+// Time: a CTA (128 threads, 256/NQ channels of one batch row, 2 per SM) walks its
 // checkpoint chunks last to first in 8-step sub-chunks. A sub-chunk is
 // rebuilt from the state entering it (all 8 decays kept, states of steps 4..7
 // kept), walked over steps 7..5, its steps 0..3 recomputed from the entry
@@ -34,8 +37,8 @@
 // pre-pass over the chunk into shared-memory slots.
 //
 // Staging: one item per sub-chunk visit (pre-pass or walk), in the order the
-// CTA consumes them, by six TMA tile loads (x, dt, dy boxes of 64 channels x
-// 8 steps, B and C boxes, and the 64 x 16 checkpoint slab the chunk starts
+// CTA consumes them, by six TMA tile loads (x, dt, dy boxes of the CTA's
+// channels x 8 steps, B and C boxes, and the channels x 4*NQ checkpoint slab the chunk starts
 // from, read at chunk -1 as zeros for the first chunk) issued by one thread
 // two items ahead, completing on per-stage mbarriers, three stages.
 // Out-of-range steps, channels and states arrive as zeros, which makes them
@@ -74,29 +77,44 @@ namespace {
 
 constexpr int CP_THREADS = 128;
 constexpr int CP_WARPS = CP_THREADS / 32;
-constexpr int CP_DPB = 64;                    // channels per CTA
 constexpr int CP_SUB = 8;                     // steps per sub-chunk
 constexpr int CP_NAT = 3;                     // TMA stages
 constexpr int CP_MAXM = 8;                    // sub-chunks per chunk (K <= 64)
 constexpr float CP_LN2 = 0.6931471805599453f;
 
+// Geometry for NQ lanes per channel pair (4 states each).
+template <int NQ>
+struct CpGeo {
+    static_assert(NQ == 4 || NQ == 8 || NQ == 16, "4, 8 or 16 lanes per channel pair");
+    static constexpr int LOGQ = NQ == 4 ? 2 : NQ == 8 ? 3 : 4;
+    static constexpr int DPB = 2 * CP_THREADS / NQ;        // channels per CTA
+    static constexpr int NP = 4 * NQ;                       // states, padded
+    static constexpr int PPW = 32 / NQ;                     // channel pairs per warp
+    static constexpr int TAUS = NQ == 16 ? 2 : 4;           // state orders in use
+    static constexpr int DUP_STEP = 2 * TAUS * NQ * 4;      // duplicated B (or C) per step
+    static constexpr int DUP = 2 * CP_SUB * DUP_STEP;       // both arrays
+    static constexpr int SD = CP_SUB * CP_WARPS * 2 * NP;   // per-warp dB|dC sums
+};
+
 // Stage layout (floats from the stage start, every region 128-byte aligned):
-// x, dt, dy [8][64] of E, B, C [8][16], entry slab [64][16].
-template <typename E>
+// x, dt, dy [8][DPB] of E, B, C [8][NP], entry slab [DPB][NP].
+template <typename E, int NQ>
 struct CpTile {
-    static constexpr int ARR = CP_SUB * CP_DPB * (int)sizeof(E) / 4;
+    using G = CpGeo<NQ>;
+    static constexpr int ARR = CP_SUB * G::DPB * (int)sizeof(E) / 4;
     static constexpr int BC = 3 * ARR;
-    static constexpr int CK = BC + 2 * CP_SUB * 16;
-    static constexpr int F = CK + CP_DPB * 16;
+    static constexpr int CK = BC + 2 * CP_SUB * G::NP;
+    static constexpr int F = CK + G::DPB * G::NP;
     static constexpr uint32_t BYTES = 4u * F;
 };
 
 struct CpSmem {
-    static constexpr int SD = CP_SUB * CP_WARPS * 32;       // per-warp dB|dC sums
     static constexpr int SLOT = CP_THREADS * 8;             // one entry state per thread
-    template <typename E>
+    template <typename E, int NQ>
     static size_t bytes(int m) {
-        return sizeof(float) * ((size_t)CP_NAT * CpTile<E>::F + 2 * CP_SUB * 128 + SD + (size_t)(m - 1) * SLOT) + 64;
+        using G = CpGeo<NQ>;
+        return sizeof(float) * ((size_t)CP_NAT * CpTile<E, NQ>::F + G::DUP + G::SD +
+                                (size_t)(m - 1) * SLOT) + 64;
     }
 };
 
@@ -126,18 +144,21 @@ __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16 *p) {
 // x, dy and dt*x) are natural pairs loaded by one 8-byte read, and the packed
 // FFMA2 / FMUL2 instructions take two elements per issue; B and C, which are
 // per state, come pre-duplicated from shared memory.
+template <int NQ>
 struct CpLane {
-    int lane, q, tau, pr;
+    int lane, q, tau, ti, pr;     // ti: index of the order tau among the orders in use
     int d0c;                      // channel 0 of the pair
     bool dv0, dv1;
     float2 nan[4];                // -Aneg*log2(e) of state s(m), (channel 0, channel 1)
     __device__ CpLane(const float *aneg, int D, int N, bool proj) {
+        using G = CpGeo<NQ>;
         const int tid = threadIdx.x;
         lane = tid & 31;
-        q = lane & 3;
-        tau = (((lane >> 4) & 1) << 1) | ((lane >> 3) & 1);
-        pr = (tid >> 5) * 8 + (lane >> 2);
-        d0c = blockIdx.x * CP_DPB + 2 * pr;
+        q = lane & (NQ - 1);
+        tau = (((lane >> 4) & 1) << 1) | (NQ <= 8 ? (lane >> 3) & 1 : 0);
+        ti = NQ == 16 ? tau >> 1 : tau;
+        pr = (tid >> 5) * G::PPW + (lane >> G::LOGQ);
+        d0c = blockIdx.x * G::DPB + 2 * pr;
         dv0 = d0c < D;
         dv1 = d0c + 1 < D;
 #pragma unroll
@@ -160,35 +181,37 @@ struct St8 {
     float2 v[4];
 };
 
-// B and C of the 8 steps duplicated per state, in the four lane state
-// orders: [a (B, C)][t][half][tau][q][4] holds (B_s(2h), B_s(2h), B_s(2h+1),
+// B and C of the 8 steps duplicated per state, in the lane state orders:
+// [a (B, C)][t][half][ti][q][4] holds (B_s(2h), B_s(2h), B_s(2h+1),
 // B_s(2h+1)) of lane (q, tau) at half h; a warp's 16-byte reads of one half
-// touch 16 consecutive 16-byte pieces (no bank conflicts).
-constexpr int CP_DUP_STEP = 2 * 4 * 4 * 4;              // floats per step and array
-constexpr int CP_DUP = 2 * CP_SUB * CP_DUP_STEP;        // both arrays, 2048 floats
-
-template <typename E>
+// touch consecutive 16-byte pieces (no bank conflicts).
+template <typename E, int NQ>
 struct CpView {
-    const E *x, *dt, *dy;        // channel pair of this lane, step stride CP_DPB
-    const float *B, *C;          // this lane's duplicated rows, step stride CP_DUP_STEP
-    const float *ck;             // entry slab [64][16]
-    __device__ CpView(const float *st, const float *dup, const CpLane &L) {
+    using G = CpGeo<NQ>;
+    const E *x, *dt, *dy;        // channel pair of this lane, step stride DPB
+    const float *B, *C;          // this lane's duplicated rows, step stride DUP_STEP
+    const float *ck;             // entry slab [DPB][NP]
+    __device__ CpView(const float *st, const float *dup, const CpLane<NQ> &L) {
         x = reinterpret_cast<const E *>(st) + 2 * L.pr;
-        dt = reinterpret_cast<const E *>(st + CpTile<E>::ARR) + 2 * L.pr;
-        dy = reinterpret_cast<const E *>(st + 2 * CpTile<E>::ARR) + 2 * L.pr;
-        B = dup + L.tau * 16 + 4 * L.q;
-        C = B + CP_SUB * CP_DUP_STEP;
-        ck = st + CpTile<E>::CK;
+        dt = reinterpret_cast<const E *>(st + CpTile<E, NQ>::ARR) + 2 * L.pr;
+        dy = reinterpret_cast<const E *>(st + 2 * CpTile<E, NQ>::ARR) + 2 * L.pr;
+        B = dup + (L.ti * NQ + L.q) * 4;
+        C = B + CP_SUB * G::DUP_STEP;
+        ck = st + CpTile<E, NQ>::CK;
     }
-    __device__ float2 xs(int t) const { return ld_pair(x + t * CP_DPB); }
-    __device__ float2 dts(int t) const { return ld_pair(dt + t * CP_DPB); }
-    __device__ float2 dys(int t) const { return ld_pair(dy + t * CP_DPB); }
+    __device__ float2 xs(int t) const { return ld_pair(x + t * G::DPB); }
+    __device__ float2 dts(int t) const { return ld_pair(dt + t * G::DPB); }
+    __device__ float2 dys(int t) const { return ld_pair(dy + t * G::DPB); }
     // (B_s(2h), B_s(2h), B_s(2h+1), B_s(2h+1))
-    __device__ float4 Bs(int t, int h) const { return *reinterpret_cast<const float4 *>(B + t * CP_DUP_STEP + h * 64); }
-    __device__ float4 Cs(int t, int h) const { return *reinterpret_cast<const float4 *>(C + t * CP_DUP_STEP + h * 64); }
+    __device__ float4 Bs(int t, int h) const {
+        return *reinterpret_cast<const float4 *>(B + t * G::DUP_STEP + h * 4 * G::TAUS * NQ);
+    }
+    __device__ float4 Cs(int t, int h) const {
+        return *reinterpret_cast<const float4 *>(C + t * G::DUP_STEP + h * 4 * G::TAUS * NQ);
+    }
     // the chunk's entry state from the checkpoint slab
-    __device__ void entry(St8 &h, const CpLane &L) const {
-        const float *r0 = ck + (2 * L.pr) * 16, *r1 = r0 + 16;
+    __device__ void entry(St8 &h, const CpLane<NQ> &L) const {
+        const float *r0 = ck + (2 * L.pr) * G::NP, *r1 = r0 + G::NP;
 #pragma unroll
         for (int m = 0; m < 4; ++m) h.v[m] = f2(r0[L.state(m)], r1[L.state(m)]);
     }
@@ -199,8 +222,9 @@ __device__ __forceinline__ float2 dup_of(const float4 &lo4, const float4 &hi4, i
 }
 
 // h <- one step; the step's dA returned in dA.
-template <typename E>
-__device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E> &v, const CpLane &L, int t) {
+template <typename E, int NQ>
+__device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E, NQ> &v, const CpLane<NQ> &L,
+                                           int t) {
     const float2 dt2 = v.dts(t);
     const float2 bx2 = mul2(dt2, v.xs(t));
     const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
@@ -212,8 +236,8 @@ __device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E> &v, 
 }
 
 // h <- one step with a known dA (no ex2).
-template <typename E>
-__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E> &v, int t) {
+template <typename E, int NQ>
+__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E, NQ> &v, int t) {
     const float2 bx2 = mul2(v.dts(t), v.xs(t));
     const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
 #pragma unroll
@@ -222,12 +246,13 @@ __device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E>
 
 // One backward step t: hc = h_t, hp = h_{t-1}, dA = dA_t; r carries
 // dA_{t+1}*g_{t+1} in and dA_t*g_t out.
-template <typename E, bool PROJ>
-__device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L, const St8 &hc,
+template <typename E, int NQ, bool PROJ>
+__device__ __forceinline__ void cp_walk_step(const CpView<E, NQ> &v, const CpLane<NQ> &L, const St8 &hc,
                                              const St8 &hp, const St8 &dA, St8 &r, St8 &dac, int t,
                                              int nv, E *outp, int D, float *sd, int warp,
                                              const Proj &pj)
 {
+    using G = CpGeo<NQ>;
     const float2 dt2 = v.dts(t), x2 = v.xs(t), dy2 = v.dys(t);
     const float2 bx2 = mul2(dt2, x2);
     const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1), C0 = v.Cs(t, 0), C1 = v.Cs(t, 1);
@@ -244,7 +269,7 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
         P[m] = f2(pb.x + pb.y, pc.x + pc.y);
         r.v[m] = rn;
     }
-    {   // dx = dt*sum gB, ddt = x*sum gB + ln2*sum nan*u, over the pair's 4 state lanes
+    {   // dx = dt*sum gB, ddt = x*sum gB + ln2*sum nan*u, over the pair's NQ state lanes
         const float2 pdx = mul2(dt2, sB);
         const float2 pddt = fma2(x2, sB, mul2(f2(CP_LN2, CP_LN2), sA));
         const bool b0 = L.lane & 1, b1 = (L.lane >> 1) & 1;
@@ -253,28 +278,41 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E> &v, const CpLane &L
         kd += __shfl_xor_sync(0xffffffffu, b0 ? pddt.x : pddt.y, 1);
         float kv = b1 ? kd : kx;
         kv += __shfl_xor_sync(0xffffffffu, b1 ? kx : kd, 2);
+        if constexpr (NQ >= 8) kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+        if constexpr (NQ >= 16) kv += __shfl_xor_sync(0xffffffffu, kv, 8);
         // this lane ends with channel b0, kind b1 (0 dx, 1 ddt); outp points at
-        // its own output array and channel
+        // its own output array and channel; lanes with q < 4 store
         if (PROJ && b1) {
             const float dtv = b0 ? dt2.y : dt2.x;
             kv *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
         }
-        if (t < nv && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
+        if (t < nv && (NQ == 4 || L.q < 4) && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
     }
-    // dB | dC over the warp's 8 channel pairs: lane bits 4, 3 select-free, bit 2 by kind
+    // dB | dC over the warp's channel pairs: lane bit 4 (and 3 for NQ <= 8)
+    // select-free, then lane bit 2 by kind for NQ = 4
     P[0] = add2(P[0], shfl2(P[2], 16));
     P[1] = add2(P[1], shfl2(P[3], 16));
-    P[0] = add2(P[0], shfl2(P[1], 8));
-    const int kb = (L.lane >> 2) & 1;
-    float kk = kb ? P[0].y : P[0].x;
-    kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 4);
-    sd[(t * CP_WARPS + warp) * 32 + kb * 16 + L.state(0)] = kk;
+    float *row = sd + (t * CP_WARPS + warp) * 2 * G::NP;
+    if constexpr (NQ <= 8) P[0] = add2(P[0], shfl2(P[1], 8));
+    if constexpr (NQ == 4) {
+        const int kb = (L.lane >> 2) & 1;
+        float kk = kb ? P[0].y : P[0].x;
+        kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 4);
+        row[kb * G::NP + L.state(0)] = kk;
+    } else {
+        row[L.state(0)] = P[0].x;
+        row[G::NP + L.state(0)] = P[0].y;
+        if constexpr (NQ == 16) {
+            row[L.state(1)] = P[1].x;
+            row[G::NP + L.state(1)] = P[1].y;
+        }
+    }
 }
 
 // The state entering sub-chunk j of a chunk: the checkpoint slab (j == 0) or
 // the pre-pass slot (j > 0).
-template <typename E>
-__device__ __forceinline__ void cp_entry(St8 &h, const CpView<E> &v, const CpLane &L, int j,
+template <typename E, int NQ>
+__device__ __forceinline__ void cp_entry(St8 &h, const CpView<E, NQ> &v, const CpLane<NQ> &L, int j,
                                          const float *slot_in)
 {
     if (j == 0) {
@@ -293,35 +331,35 @@ __device__ __forceinline__ void cp_entry(St8 &h, const CpView<E> &v, const CpLan
 // carry r. All 8 decays are kept; of the states only h_4..h_7, and h_{-1}..h_3
 // are recomputed from the entry state with the kept decays (no ex2) when the
 // walk reaches them, which keeps the live registers low.
-template <typename E, bool PROJ>
-__device__ __forceinline__ void cp_walk(const CpView<E> &v, const CpLane &L, int j,
+template <typename E, int NQ, bool PROJ>
+__device__ __forceinline__ void cp_walk(const CpView<E, NQ> &v, const CpLane<NQ> &L, int j,
                                         const float *slot_in, St8 &r, St8 &dac, int nv, E *outp,
                                         int D, float *sd, int warp, const Proj &pj)
 {
     St8 dA[CP_SUB], hk[4];                // hk[t - 4] = h_t
     {
         St8 h;
-        cp_entry<E>(h, v, L, j, slot_in);
+        cp_entry<E, NQ>(h, v, L, j, slot_in);
 #pragma unroll
         for (int t = 0; t < CP_SUB; ++t) {
-            cp_advance<E>(h, dA[t], v, L, t);
+            cp_advance<E, NQ>(h, dA[t], v, L, t);
             if (t >= 4) hk[t - 4] = h;
         }
     }
 #pragma unroll
     for (int t = CP_SUB - 1; t >= 5; --t)
-        cp_walk_step<E, PROJ>(v, L, hk[t - 4], hk[t - 5], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+        cp_walk_step<E, NQ, PROJ>(v, L, hk[t - 4], hk[t - 5], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
     St8 hl[5];                            // hl[t + 1] = h_t for t = -1 .. 3
-    cp_entry<E>(hl[0], v, L, j, slot_in);
+    cp_entry<E, NQ>(hl[0], v, L, j, slot_in);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         hl[t + 1] = hl[t];
-        cp_replay<E>(hl[t + 1], dA[t], v, t);
+        cp_replay<E, NQ>(hl[t + 1], dA[t], v, t);
     }
-    cp_walk_step<E, PROJ>(v, L, hk[0], hl[4], dA[4], r, dac, 4, nv, outp, D, sd, warp, pj);
+    cp_walk_step<E, NQ, PROJ>(v, L, hk[0], hl[4], dA[4], r, dac, 4, nv, outp, D, sd, warp, pj);
 #pragma unroll
     for (int t = 3; t >= 0; --t)
-        cp_walk_step<E, PROJ>(v, L, hl[t + 1], hl[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+        cp_walk_step<E, NQ, PROJ>(v, L, hl[t + 1], hl[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
 }
 
 // The item sequence of one CTA: chunks chi down to clo; in a chunk with mv
@@ -344,7 +382,7 @@ struct CpCursor {
     }
 };
 
-template <typename E, bool PROJ>
+template <typename E, int NQ, bool PROJ>
 __global__ void __launch_bounds__(CP_THREADS, MMS_BWD_CP_MINB)
 bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict__ ddt,
               float *__restrict__ part_bc, float *__restrict__ part_a,
@@ -353,21 +391,22 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 {
     Proj pj = pj_in;
     pj.on = PROJ;
-    using Q = CpTile<E>;
+    using G = CpGeo<NQ>;
+    using Q = CpTile<E, NQ>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;                                  // [CP_NAT][Q::F]
-    float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (CP_DUP)
-    float *sd = dup + CP_DUP;                              // [8][4][32]
-    float *slots = sd + CpSmem::SD;                        // [M-1][128][8]
+    float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (G::DUP)
+    float *sd = dup + G::DUP;                              // [8][4 warps][2 NP]
+    float *slots = sd + G::SD;                             // [M-1][128][8]
     const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * CpSmem::SLOT);
 
-    const CpLane L(aneg, D, N, PROJ);
+    const CpLane<NQ> L(aneg, D, N, PROJ);
     const int tid = threadIdx.x, brow = blockIdx.y;
     const int K = M * CP_SUB;
     const int nchunk = (T + K - 1) / K;
     const size_t plane = (size_t)D * N;
     const size_t rowD = (size_t)brow * T * D;
-    const int d0 = blockIdx.x * CP_DPB;
+    const int d0 = blockIdx.x * G::DPB;
     float *pbc = part_bc + ((size_t)brow * nblk + blockIdx.x) * T * 2 * N;
 
     const int sg = blockIdx.z, nsg = gridDim.z;
@@ -385,7 +424,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         tma3(dst + 4 * Q::ARR, &maps.dt, d0, t0, brow, bar);
         tma3(dst + 8 * Q::ARR, &maps.dy, d0, t0, brow, bar);
         tma3(dst + 4 * Q::BC, &maps.B, 0, t0, brow, bar);
-        tma3(dst + 4 * (Q::BC + CP_SUB * 16), &maps.C, 0, t0, brow, bar);
+        tma3(dst + 4 * (Q::BC + CP_SUB * G::NP), &maps.C, 0, t0, brow, bar);
         tma4(dst + 4 * Q::CK, &maps.ck, 0, d0, at.c - 1, brow, bar);
     };
 
@@ -412,26 +451,29 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     }
     __syncthreads();
 
-    // this thread's share of the dB|dC flush: rows fr and fr + 4 of a walked
-    // sub-chunk, column fj of the four warps' sums
-    const int fr = tid >> 5, fj = tid & 31;
-    const bool fvalid = (fj & 15) < N;
-    float *pbc_col = pbc + (fj >> 4) * N + (fj & 15);
+    // this thread's share of the dB|dC flush: rows fr, fr + RPP, ... of a
+    // walked sub-chunk, column fj of the four warps' sums
+    constexpr int COLS = 2 * G::NP, RPP = CP_THREADS / COLS;
+    const int fr = tid / COLS, fj = tid % COLS;
+    const bool fvalid = fj % G::NP < N;
+    float *pbc_col = pbc + (fj / G::NP) * N + fj % G::NP;
     auto flush = [&](int t0p, int nvp) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const int i = fr + 4 * h;
+        for (int h = 0; h < CP_SUB / RPP; ++h) {
+            const int i = fr + RPP * h;
             if (i < nvp && fvalid) {
-                const float *q = sd + i * CP_WARPS * 32 + fj;
-                pbc_col[(size_t)(t0p + i) * 2 * N] = (q[0] + q[32]) + (q[64] + q[96]);
+                const float *q = sd + i * CP_WARPS * COLS + fj;
+                pbc_col[(size_t)(t0p + i) * 2 * N] = (q[0] + q[COLS]) + (q[2 * COLS] + q[3 * COLS]);
             }
         }
     };
-    // this thread's share of the B, C duplication: lane order pta, quad pq,
-    // half ph, steps pt and pt + 4
-    const int pq = tid & 3, pta = (tid >> 2) & 3, ph = (tid >> 4) & 1, pt = tid >> 5;
-    const int ps0 = 4 * pq + ((2 * ph) ^ pta), ps1 = 4 * pq + ((2 * ph + 1) ^ pta);
-    const int pdst = ((ph * 4 + pta) * 4 + pq) * 4;
+    // this thread's share of the B, C duplication: combination pc = (half,
+    // order, quad) of a step, rows pat, pat + GRP, ... of the 16 (array, step) rows
+    constexpr int CMB = 2 * G::TAUS * NQ, GRP = CP_THREADS / CMB;
+    const int pc = tid % CMB, pat = tid / CMB;
+    const int pq = pc % NQ, pti = (pc / NQ) % G::TAUS, ph = pc / (NQ * G::TAUS);
+    const int ptau = NQ == 16 ? pti << 1 : pti;
+    const int ps0 = 4 * pq + ((2 * ph) ^ ptau), ps1 = 4 * pq + ((2 * ph + 1) ^ ptau);
 
     CpCursor cur(chi, M, T, K, nchunk);
     int pend_t0 = -1, pend_nv = 0;
@@ -455,20 +497,17 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
             flush(pend_t0, pend_nv);
             pend_t0 = -1;
         }
-        // B, C of the 8 steps duplicated per state in the four lane orders
+        // B, C of the 8 steps duplicated per state in the lane orders
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int tt = 0; tt < 2; ++tt) {
-                const int t = pt + 4 * tt;
-                const float *src = st + Q::BC + (a * CP_SUB + t) * 16;
-                const float b0 = src[ps0], b1 = src[ps1];
-                *reinterpret_cast<float4 *>(dup + (a * CP_SUB + t) * CP_DUP_STEP + pdst) =
-                    make_float4(b0, b0, b1, b1);
-            }
+        for (int k = 0; k < 2 * CP_SUB / GRP; ++k) {
+            const int at = pat + GRP * k;                  // array at / 8, step at % 8
+            const float *src = st + Q::BC + at * G::NP;
+            const float b0 = src[ps0], b1 = src[ps1];
+            *reinterpret_cast<float4 *>(dup + at * G::DUP_STEP + 4 * pc) = make_float4(b0, b0, b1, b1);
+        }
         if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
             float *dts = st + Q::ARR;
-            for (int e = tid; e < CP_SUB * CP_DPB; e += CP_THREADS)
+            for (int e = tid; e < CP_SUB * G::DPB; e += CP_THREADS)
                 dts[e] = fmaf(pj.range, sigmoid_fast(dts[e]), pj.lo);
         }
         if (tid == 0 && i + 2 < total) {
@@ -478,7 +517,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         }
         __syncthreads();
 
-        const CpView<E> v(st, dup, L);
+        const CpView<E, NQ> v(st, dup, L);
         const int u = c * M + j;                           // sub-chunk index in the sequence
         const int t0 = u * CP_SUB;
         const int nv = min(CP_SUB, T - t0);
@@ -486,16 +525,16 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         if (!walk) {
             // pre-pass: the state entering sub-chunk j+1 into slot j
             St8 h, dA;
-            cp_entry<E>(h, v, L, j, slot_in);
+            cp_entry<E, NQ>(h, v, L, j, slot_in);
 #pragma unroll
-            for (int t = 0; t < CP_SUB; ++t) cp_advance<E>(h, dA, v, L, t);
+            for (int t = 0; t < CP_SUB; ++t) cp_advance<E, NQ>(h, dA, v, L, t);
             float4 *sl = reinterpret_cast<float4 *>(slots + (size_t)j * CpSmem::SLOT + tid * 8);
             sl[0] = make_float4(h.v[0].x, h.v[0].y, h.v[1].x, h.v[1].y);
             sl[1] = make_float4(h.v[2].x, h.v[2].y, h.v[3].x, h.v[3].y);
         } else {
             // this lane's output after the dx / ddt exchange: array (lane bit 1), channel (bit 0)
             E *outp = ((L.lane >> 1) & 1 ? ddt : dx) + rowD + (size_t)t0 * D + L.d0c + (L.lane & 1);
-            cp_walk<E, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
+            cp_walk<E, NQ, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
             pend_t0 = t0;
             pend_nv = nv;
         }
@@ -518,58 +557,73 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     }
 }
 
+template <int NQ>
 bool build_cp_maps(const BwdArgs &a, CpMaps *m)
 {
+    using G = CpGeo<NQ>;
     const auto fn = tma_encoder();
     if (!fn || !tma_context()) return false;
     const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
-    const cuuint32_t bX[3] = {CP_DPB, CP_SUB, 1};
+    const cuuint32_t bX[3] = {G::DPB, CP_SUB, 1};
     const cuuint64_t dB[3] = {(cuuint64_t)a.N, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
-    const cuuint32_t bB[3] = {16, CP_SUB, 1};
+    const cuuint32_t bB[3] = {G::NP, CP_SUB, 1};
     const int nchunk = (a.T + a.K - 1) / a.K;
     const cuuint64_t dK[4] = {(cuuint64_t)a.N, (cuuint64_t)a.D, (cuuint64_t)nchunk, (cuuint64_t)a.Bt};
-    const cuuint32_t bK[4] = {16, CP_DPB, 1, 1};
+    const cuuint32_t bK[4] = {G::NP, G::DPB, 1, 1};
     const int ex = a.bf16 ? 2 : 4;
     return tma_encode(fn, &m->x, a.x, 3, dX, bX, ex) && tma_encode(fn, &m->dt, a.dt, 3, dX, bX, ex) &&
            tma_encode(fn, &m->dy, a.dy, 3, dX, bX, ex) && tma_encode(fn, &m->B, a.B, 3, dB, bB) &&
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
-template <typename E, bool PROJ>
+template <typename E, int NQ, bool PROJ>
 cudaError_t launch_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
-                      int nblk, SegPlan sp, const CpMaps &maps, cudaStream_t stream)
+                      int nblk, SegPlan sp, cudaStream_t stream)
 {
+    CpMaps maps;
+    memset(&maps, 0, sizeof(maps));
+    if (!build_cp_maps<NQ>(a, &maps)) return cudaErrorInvalidValue;
     const int M = a.K / CP_SUB;
-    const size_t smem = CpSmem::bytes<E>(CP_MAXM);         // one opt-in size for every M
-    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, PROJ>>(smem);
+    const size_t smem = CpSmem::bytes<E, NQ>(CP_MAXM);     // one opt-in size for every M
+    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, NQ, PROJ>>(smem);
     if (e != cudaSuccess) return e;
     const uint32_t limit = tma_wait_limit();
     const int skip = tma_skip_item();
-    dim3 grid((a.D + CP_DPB - 1) / CP_DPB, a.Bt, sp.S);
-    bwd_kernel_cp<E, PROJ><<<grid, CP_THREADS, CpSmem::bytes<E>(M), stream>>>(
+    dim3 grid((a.D + CpGeo<NQ>::DPB - 1) / CpGeo<NQ>::DPB, a.Bt, sp.S);
+    bwd_kernel_cp<E, NQ, PROJ><<<grid, CP_THREADS, CpSmem::bytes<E, NQ>(M), stream>>>(
         a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,
         a.T, a.D, a.N, M, nblk, sp.cps, maps, a.proj, limit, skip);
     return cudaGetLastError();
+}
+
+template <int NQ>
+cudaError_t launch_cp_n(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                        int nblk, SegPlan sp, cudaStream_t stream)
+{
+    return a.proj.on ? launch_cp<float, NQ, true>(a, part_bc, part_a, seg_e, nblk, sp, stream)
+                     : launch_cp<float, NQ, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
 }
 
 }  // namespace
 
 bool bwd_cp_applies(const BwdArgs &a)
 {
-    if (!cp_shape(a.N, a.K) || (a.K == CP_SUB && !MMS_BWD_CP_K8)) return false;
-
-    if (a.bf16) return false;              // bf16 stays on the 8-state kernel (mms_bwd_w8.cu)
+    if (!cp_shape(a.N, a.K)) return false;
+    // stride 8 at 8 < N <= 16 runs the 8-state kernel (mms_bwd_w8.cu) unless MMS_BWD_CP_K8
+    if (w8_shape(a.N, a.K) && !MMS_BWD_CP_K8) return false;
+    if (a.bf16) return false;              // bf16 runs the 8-state or G-lane kernels
     return vec_ok(a.D, a.x, a.dt, a.dy);
 }
 
 cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                           int nblk, SegPlan sp, cudaStream_t stream)
 {
-    CpMaps maps;
-    memset(&maps, 0, sizeof(maps));
-    if (!build_cp_maps(a, &maps)) return cudaErrorInvalidValue;
-    return a.proj.on ? launch_cp<float, true>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream)
-                     : launch_cp<float, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
+    switch (groups_for(a.N)) {
+    case 4: return launch_cp_n<4>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 8: return launch_cp_n<8>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 16: return launch_cp_n<16>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 int cp_take_timeout()

@@ -90,9 +90,9 @@ struct SegPlan {
 
 // The shapes of the 8-state backward (mms_bwd_w8.cu): 8 < N <= 16, K == 8.
 inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8; }
-// The shapes of the channel-pair backward (mms_bwd_cp.cu): 8 < N <= 16,
+// The shapes of the channel-pair backward (mms_bwd_cp.cu): 8 < N <= 64,
 // K a multiple of 8 up to 64.
-inline bool cp_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K % 8 == 0 && K <= 64; }
+inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64; }
 
 // Bounded waits of the TMA-staged kernels: polls of one stage's completion
 // barrier before a kernel gives up (default 2^22), and a staged item whose

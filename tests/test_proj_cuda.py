@@ -33,6 +33,8 @@ CASES = [
     (2, 130, 33, 16, 8),       # D % 4 != 0: cp.async paths
     (3, 64, 20, 12, 8),        # d_state 12
     (2, 77, 21, 32, 64),       # d_state 32, stride 64 (4-state backward, recompute)
+    (2, 100, 64, 32, 8),       # d_state 32: channel-pair backward, 8 lanes per pair
+    (1, 150, 48, 64, 16),      # d_state 64: channel-pair backward, 16 lanes per pair
     (1, 200, 40, 8, 7),        # d_state 8, stride 7
     (1, 3000, 64, 16, 8),      # long: many time segments
 ]

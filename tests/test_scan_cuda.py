@@ -123,6 +123,24 @@ def test_long_sequences_match_the_float64_oracle(bt, t_len, d, n, chunk, slow):
     assert max_rel(ckpt, ckpt64) <= FWD_TOL
 
 
+# The channel-pair backward at d_state 20..64 (8 or 16 lanes per channel
+# pair): every stride class, a channel count that leaves a CTA partly empty,
+# and a long sequence that also runs time segments.
+PAIRS = [(2, 200, 64, 32, 8, False), (1, 333, 48, 20, 16, False), (2, 150, 40, 48, 24, False),
+         (1, 257, 32, 64, 64, False), (1, 100, 36, 64, 8, False), (2, 130, 24, 28, 40, False),
+         (1, 3000, 96, 32, 16, True), (1, 2500, 32, 64, 8, True)]
+
+
+@pytest.mark.parametrize("bt,t_len,d,n,chunk,slow", PAIRS)
+def test_channel_pair_backward_at_wide_state_matches_the_float64_oracle(bt, t_len, d, n, chunk, slow):
+    x, dt, aneg, b_in, c_in, dy = inputs(bt, t_len, d, n, "c0", seed=7 * t_len + n, device=DEV)
+    if slow:
+        dt = dt * 0.02
+    y, grads = cuda_fwd_bwd(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    y64, _, g64 = oracle64(x, dt, aneg, b_in, c_in, dy, chunk=chunk)
+    assert_parity(y, grads, y64, g64, f"{(bt, t_len, d, n)} chunk {chunk} slow {slow}")
+
+
 def test_config3_shape_matches_the_float64_oracle():
     """One sequence of config 3 per GPU: B=1, T=16384, d_inner=2048, d_state=16."""
     x, dt, aneg, b_in, c_in, dy = inputs(1, 16384, 2048, 16, "c0", seed=3, device=DEV)
