@@ -600,6 +600,7 @@ template <int NQ>
 cudaError_t launch_cp_n(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                         int nblk, SegPlan sp, cudaStream_t stream)
 {
+    if (a.bf16) return launch_cp<__nv_bfloat16, NQ, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
     return a.proj.on ? launch_cp<float, NQ, true>(a, part_bc, part_a, seg_e, nblk, sp, stream)
                      : launch_cp<float, NQ, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
 }
@@ -609,9 +610,11 @@ cudaError_t launch_cp_n(const BwdArgs &a, float *part_bc, float *part_a, const f
 bool bwd_cp_applies(const BwdArgs &a)
 {
     if (!cp_shape(a.N, a.K)) return false;
-    // stride 8 at 8 < N <= 16 runs the 8-state kernel (mms_bwd_w8.cu) unless MMS_BWD_CP_K8
-    if (w8_shape(a.N, a.K) && !MMS_BWD_CP_K8) return false;
-    if (a.bf16) return false;              // bf16 runs the 8-state or G-lane kernels
+    // stride 8 at 8 < N <= 16 runs the 8-state kernel (mms_bwd_w8.cu), bf16
+    // always and fp32 unless MMS_BWD_CP_K8: bf16 and fp32 run the same kernel
+    // on a shape, so bf16 storage only rounds the fp32 results
+    if (w8_shape(a.N, a.K) && (!MMS_BWD_CP_K8 || a.bf16)) return false;
+    if (a.bf16 && (a.D % 8 != 0 || a.proj.on)) return false;
     return vec_ok(a.D, a.x, a.dt, a.dy);
 }
 
