@@ -101,6 +101,17 @@ def launches_per_step(bt, t_len, d, n, k):
     return 3 + 2 * split_f + 2 * split_b
 
 
+def bwd_kernel_label(n, k, d):
+    """The backward kernel the library runs on (N, K, D) with aligned fp32 arrays."""
+    if 8 < n <= 16 and k == 8:
+        name = "bwd_kernel_w8"
+    elif 8 < n <= 64 and k % 8 == 0 and k <= 64 and d % 4 == 0:
+        name = "bwd_kernel_cp"
+    else:
+        name = "bwd_kernel_k8" if k == 8 else "bwd_kernel"
+    return f"mms_bwd ({name} + reduce_kernel)"
+
+
 def workload_config(name, shape, world, channel, d_local):
     """The `config` object both arms print (the driver compares them key by key)."""
     bt, t_len, d_total, n, kk = shape
@@ -409,8 +420,7 @@ def run_native(args, shape):
     tfile = REPO / "profiles" / "traffic.json"
     if tfile.exists() and kk == 8:                          # captured at the default stride
         traffic = json.loads(tfile.read_text()).get(f"{args.config}_bwd_bytes_per_launch")
-    roof = kernel_roofline("mms_bwd (bwd_kernel_w8 + reduce_kernel)" if kk == 8 else
-                           "mms_bwd (bwd_kernel_cp + reduce_kernel)", bwd_ms * 1e-3, bwd_b, bdn,
+    roof = kernel_roofline(bwd_kernel_label(n, kk, d), bwd_ms * 1e-3, bwd_b, bdn,
                            hbm_gbs, ex2_per_s, BWD_FP32_LANES_PER_STATE_STEP * bdn, ffma_per_s)
     roof["traffic"] = traffic
     roof["peak_source"] = (f"HBM: {peak_kind} (MEASURED_PEAKS.json hbm_gbs); MUFU: measured in this "
@@ -437,7 +447,7 @@ def run_native(args, shape):
         t64 = (s64["fwd_ms"] + s64["bwd_ms"]) * 1e-3
         s64["step_roofline"] = step_roofline(t64, fwd_b + bwd_b, 2 * bdn, hbm_gbs, ex2_per_s,
                                              rates, sm_mhz, sm_max_default)
-        s64["roofline"] = kernel_roofline("mms_bwd (bwd_kernel_cp + reduce_kernel)",
+        s64["roofline"] = kernel_roofline(bwd_kernel_label(n, 64, d),
                                           s64["bwd_ms"] * 1e-3, bwd_b, bdn, hbm_gbs, ex2_per_s,
                                           BWD_FP32_LANES_PER_STATE_STEP * bdn, ffma_per_s)
         s64["roofline"]["note"] = ("algorithmic units as at stride 8; at stride 64 the kernel "

@@ -11,42 +11,52 @@
 //
 // Decomposition, chosen from the measured per-SM rates of this GPU (FP32 128
 // lanes/clk with packed FFMA2 no faster than FFMA, MUFU ex2 16/clk, warp
-// shuffles about 20/clk): a thread owns two adjacent channels x four states.
+// shuffles about 20/clk): a thread owns two adjacent channels x SPT states.
 //   * dB and dC are sums over channels. Holding two channels, a thread adds
-//     them with FMAs before any cross-lane work, and the warp then reduces 8
-//     values over its 8 channel pairs (7 shuffles); with dx / ddt (3 shuffles
-//     over the channel's 4 state lanes) that is 1.25 shuffles per state-step
-//     instead of 2 with one channel per thread.
+//     them before any cross-lane work; the warp then reduces over its channel
+//     pairs. At N = 16 (4 lanes per pair, 8 pairs per warp) that is 7
+//     shuffles for dB|dC and 3 for dx / ddt per 8 state-steps, 1.25 shuffles
+//     per state-step instead of 2 with one channel per thread.
 //   * The 8 decays of a sub-chunk stay in registers from the rebuild to the
 //     walk, so every state-step costs one MUFU ex2 (at K = 8).
-// Lane layout: NQ = N/4 (rounded up to 4, 8 or 16) lanes share a channel
-// pair; q = the low log2(NQ) lane bits picks states 4q..4q+3, the higher
-// lane bits the channel pair within the warp. The thread keeps its states in
-// the order 4q + (m XOR tau), tau = lane bits 4,3 (bit 4 only for NQ = 16),
-// so the butterfly levels of the dB|dC reduction over the pair bits among
-// lane bits 4 and 3 are select-free; B and C are rewritten once per
-// sub-chunk into the lane orders in shared memory. The dB|dC reduction has
-// log2(32/NQ) levels (3, 2, 1) and dx / ddt log2(NQ) (2, 3, 4).
+// Lane layout: NQ lanes share a channel pair (NQ = N / SPT rounded up to a
+// power of two); q = the low log2(NQ) lane bits picks states SPT*q ..
+// SPT*q + SPT-1, the higher lane bits the channel pair within the warp. The
+// thread keeps its states in the order SPT*q + (m XOR tau), tau from lane
+// bits 4 and 3 that are pair bits, so the butterfly levels of the dB|dC
+// reduction over those bits are select-free; B and C are rewritten once per
+// sub-chunk into the lane orders in shared memory. The lowest pair bit left,
+// if any, reduces by kind (dB on one lane, dC on its partner).
+//   SPT = 4 (the default; 128-thread CTAs, about 250 registers, 2 CTAs per SM)
+//     on NQ = 4, 8, 16 lanes for N <= 16, 32, 64;
+//   SPT = 2 (256-thread CTAs at 128 registers, 2 per SM: twice the warps) on
+//     NQ = 8, 16 lanes for N <= 16, 32, built when MMS_BWD_CP2_MAXN is set.
+//     It measures slower (config 1 at K = 8: 443 against 346 us, N = 32:
+//     897 against 670 us): per state-step it loads, shuffles and selects
+//     more than the extra warps hide.
+// Both give 256 / groups_for(N) channels per CTA, the general backward's
+// block, so they share its workspace.
 //
-// Time: a CTA (128 threads, 256/NQ channels of one batch row, 2 per SM) walks its
-// checkpoint chunks last to first in 8-step sub-chunks. A sub-chunk is
-// rebuilt from the state entering it (all 8 decays kept, states of steps 4..7
-// kept), walked over steps 7..5, its steps 0..3 recomputed from the entry
-// state with the kept decays (no ex2), and walked over steps 4..0. For K > 8
-// the states entering sub-chunks 1..m-1 of a chunk come from a forward
-// pre-pass over the chunk into shared-memory slots.
+// Time: a CTA walks its checkpoint chunks last to first in 8-step
+// sub-chunks. A sub-chunk is rebuilt from the state entering it (all 8
+// decays kept, states of steps 4..7 kept), walked over steps 7..5, its steps
+// 0..3 recomputed from the entry state with the kept decays (no ex2), and
+// walked over steps 4..0. For K > 8 the states entering sub-chunks 1..m-1 of
+// a chunk come from a forward pre-pass over the chunk into shared-memory
+// slots.
 //
 // Staging: one item per sub-chunk visit (pre-pass or walk), in the order the
 // CTA consumes them, by six TMA tile loads (x, dt, dy boxes of the CTA's
-// channels x 8 steps, B and C boxes, and the channels x 4*NQ checkpoint slab the chunk starts
-// from, read at chunk -1 as zeros for the first chunk) issued by one thread
-// two items ahead, completing on per-stage mbarriers, three stages.
+// channels x 8 steps, B and C boxes, and the channels x SPT*NQ checkpoint
+// slab the chunk starts from, read at chunk -1 as zeros for the first chunk)
+// issued by one thread two items ahead, completing on per-stage mbarriers,
+// three stages.
 // Out-of-range steps, channels and states arrive as zeros, which makes them
 // no-ops (dt = 0 gives dA = 1 and no input; dy = C = 0 give no adjoint).
 //
 // Reductions (deterministic, no float atomics): dx / ddt are finished by the
 // lane exchange above; dB / dC per warp go to shared memory and the CTA's
-// four warps are summed into one partial per CTA and step (reduce_kernel
+// warps are summed into one partial per CTA and step (reduce_kernel
 // adds the CTAs); dAneg accumulates in registers over the walk into one
 // partial per (batch row, time segment).
 //
@@ -63,58 +73,48 @@
 #include "mms_stage.cuh"
 #include "mms_tma.cuh"
 
-#ifndef MMS_BWD_CP_MINB
-#define MMS_BWD_CP_MINB 2
-#endif
-// K = 8 runs the 8-state kernel (mms_bwd_w8.cu) unless this is set.
-#ifndef MMS_BWD_CP_K8
-#define MMS_BWD_CP_K8 0
-#endif
-
 namespace mms {
 
 namespace {
 
-constexpr int CP_THREADS = 128;
-constexpr int CP_WARPS = CP_THREADS / 32;
 constexpr int CP_SUB = 8;                     // steps per sub-chunk
 constexpr int CP_NAT = 3;                     // TMA stages
 constexpr int CP_MAXM = 8;                    // sub-chunks per chunk (K <= 64)
 constexpr float CP_LN2 = 0.6931471805599453f;
 
-// Geometry for NQ lanes per channel pair (4 states each).
-template <int NQ>
+// Geometry: NQ lanes share a channel pair, each lane holding SPT states of
+// both channels (SPT = 4: 128-thread CTAs; SPT = 2: 256-thread CTAs, half the
+// registers per thread). Both give 256 / groups_for(N) channels per CTA.
+template <int NQ_, int SPT_>
 struct CpGeo {
-    static_assert(NQ == 4 || NQ == 8 || NQ == 16, "4, 8 or 16 lanes per channel pair");
+    static constexpr int NQ = NQ_, SPT = SPT_;
+    static_assert((SPT == 4 && (NQ == 4 || NQ == 8 || NQ == 16)) || (SPT == 2 && (NQ == 8 || NQ == 16)),
+                  "4 states on 4, 8 or 16 lanes, or 2 states on 8 or 16 lanes");
+    static constexpr int THREADS = 512 / SPT;
+    static constexpr int WARPS = THREADS / 32;
     static constexpr int LOGQ = NQ == 4 ? 2 : NQ == 8 ? 3 : 4;
-    static constexpr int DPB = 2 * CP_THREADS / NQ;        // channels per CTA
-    static constexpr int NP = 4 * NQ;                       // states, padded
+    static constexpr int DPB = 2 * THREADS / NQ;            // channels per CTA
+    static constexpr int NP = SPT * NQ;                     // states, padded
     static constexpr int PPW = 32 / NQ;                     // channel pairs per warp
-    static constexpr int TAUS = NQ == 16 ? 2 : 4;           // state orders in use
-    static constexpr int DUP_STEP = 2 * TAUS * NQ * 4;      // duplicated B (or C) per step
+    static constexpr int HALVES = SPT / 2;                  // float4 of duplicated B per step
+    static constexpr int TAUS = SPT == 2 || NQ == 16 ? 2 : 4;   // state orders in use
+    static constexpr int DUP_STEP = HALVES * TAUS * NQ * 4; // duplicated B (or C) per step
     static constexpr int DUP = 2 * CP_SUB * DUP_STEP;       // both arrays
-    static constexpr int SD = CP_SUB * CP_WARPS * 2 * NP;   // per-warp dB|dC sums
+    static constexpr int SD = CP_SUB * WARPS * 2 * NP;      // per-warp dB|dC sums
+    static constexpr int SLOT = THREADS * 2 * SPT;          // one entry state per thread
 };
 
 // Stage layout (floats from the stage start, every region 128-byte aligned):
 // x, dt, dy [8][DPB] of E, B, C [8][NP], entry slab [DPB][NP].
-template <typename E, int NQ>
+template <typename E, typename G>
 struct CpTile {
-    using G = CpGeo<NQ>;
     static constexpr int ARR = CP_SUB * G::DPB * (int)sizeof(E) / 4;
     static constexpr int BC = 3 * ARR;
     static constexpr int CK = BC + 2 * CP_SUB * G::NP;
     static constexpr int F = CK + G::DPB * G::NP;
     static constexpr uint32_t BYTES = 4u * F;
-};
-
-struct CpSmem {
-    static constexpr int SLOT = CP_THREADS * 8;             // one entry state per thread
-    template <typename E, int NQ>
-    static size_t bytes(int m) {
-        using G = CpGeo<NQ>;
-        return sizeof(float) * ((size_t)CP_NAT * CpTile<E, NQ>::F + G::DUP + G::SD +
-                                (size_t)(m - 1) * SLOT) + 64;
+    static size_t smem(int m) {
+        return sizeof(float) * ((size_t)CP_NAT * F + G::DUP + G::SD + (size_t)(m - 1) * G::SLOT) + 64;
     }
 };
 
@@ -144,25 +144,28 @@ __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16 *p) {
 // x, dy and dt*x) are natural pairs loaded by one 8-byte read, and the packed
 // FFMA2 / FMUL2 instructions take two elements per issue; B and C, which are
 // per state, come pre-duplicated from shared memory.
-template <int NQ>
+template <typename G>
 struct CpLane {
     int lane, q, tau, ti, pr;     // ti: index of the order tau among the orders in use
     int d0c;                      // channel 0 of the pair
     bool dv0, dv1;
-    float2 nan[4];                // -Aneg*log2(e) of state s(m), (channel 0, channel 1)
+    float2 nan[G::SPT];           // -Aneg*log2(e) of state s(m), (channel 0, channel 1)
     __device__ CpLane(const float *aneg, int D, int N, bool proj) {
-        using G = CpGeo<NQ>;
         const int tid = threadIdx.x;
         lane = tid & 31;
-        q = lane & (NQ - 1);
-        tau = (((lane >> 4) & 1) << 1) | (NQ <= 8 ? (lane >> 3) & 1 : 0);
-        ti = NQ == 16 ? tau >> 1 : tau;
+        q = lane & (G::NQ - 1);
+        if constexpr (G::SPT == 4) {
+            tau = (((lane >> 4) & 1) << 1) | (G::NQ <= 8 ? (lane >> 3) & 1 : 0);
+            ti = G::NQ == 16 ? tau >> 1 : tau;
+        } else {
+            tau = ti = (lane >> 4) & 1;
+        }
         pr = (tid >> 5) * G::PPW + (lane >> G::LOGQ);
         d0c = blockIdx.x * G::DPB + 2 * pr;
         dv0 = d0c < D;
         dv1 = d0c + 1 < D;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < G::SPT; ++m) {
             const int s = state(m);
             float a0 = dv0 && s < N ? __ldg(aneg + (size_t)d0c * N + s) : 0.f;
             float a1 = dv1 && s < N ? __ldg(aneg + (size_t)(d0c + 1) * N + s) : 0.f;
@@ -173,96 +176,108 @@ struct CpLane {
             nan[m] = f2(-a0 * MMS_LOG2E, -a1 * MMS_LOG2E);
         }
     }
-    __device__ int state(int m) const { return 4 * q + (m ^ tau); }
+    __device__ int state(int m) const { return G::SPT * q + (m ^ tau); }
 };
 
-// One thread's 8 state values: [position m] = (channel 0, channel 1) of state s(m).
-struct St8 {
-    float2 v[4];
+// One thread's state values: [position m] = (channel 0, channel 1) of state s(m).
+template <int SPT>
+struct St {
+    float2 v[SPT];
+};
+
+// The duplicated B (or C) of one step for one lane: (B_s(m), B_s(m)) at m.
+template <int SPT>
+struct DupV;
+template <>
+struct DupV<4> {
+    float4 a, b;
+    __device__ float2 operator[](int m) const { return m == 0 ? lo(a) : m == 1 ? hi(a) : m == 2 ? lo(b) : hi(b); }
+};
+template <>
+struct DupV<2> {
+    float4 a;
+    __device__ float2 operator[](int m) const { return m == 0 ? lo(a) : hi(a); }
 };
 
 // B and C of the 8 steps duplicated per state, in the lane state orders:
 // [a (B, C)][t][half][ti][q][4] holds (B_s(2h), B_s(2h), B_s(2h+1),
 // B_s(2h+1)) of lane (q, tau) at half h; a warp's 16-byte reads of one half
 // touch consecutive 16-byte pieces (no bank conflicts).
-template <typename E, int NQ>
+template <typename E, typename G>
 struct CpView {
-    using G = CpGeo<NQ>;
+    using Q = CpTile<E, G>;
     const E *x, *dt, *dy;        // channel pair of this lane, step stride DPB
     const float *B, *C;          // this lane's duplicated rows, step stride DUP_STEP
     const float *ck;             // entry slab [DPB][NP]
-    __device__ CpView(const float *st, const float *dup, const CpLane<NQ> &L) {
+    __device__ CpView(const float *st, const float *dup, const CpLane<G> &L) {
         x = reinterpret_cast<const E *>(st) + 2 * L.pr;
-        dt = reinterpret_cast<const E *>(st + CpTile<E, NQ>::ARR) + 2 * L.pr;
-        dy = reinterpret_cast<const E *>(st + 2 * CpTile<E, NQ>::ARR) + 2 * L.pr;
-        B = dup + (L.ti * NQ + L.q) * 4;
+        dt = reinterpret_cast<const E *>(st + Q::ARR) + 2 * L.pr;
+        dy = reinterpret_cast<const E *>(st + 2 * Q::ARR) + 2 * L.pr;
+        B = dup + (L.ti * G::NQ + L.q) * 4;
         C = B + CP_SUB * G::DUP_STEP;
-        ck = st + CpTile<E, NQ>::CK;
+        ck = st + Q::CK;
     }
     __device__ float2 xs(int t) const { return ld_pair(x + t * G::DPB); }
     __device__ float2 dts(int t) const { return ld_pair(dt + t * G::DPB); }
     __device__ float2 dys(int t) const { return ld_pair(dy + t * G::DPB); }
-    // (B_s(2h), B_s(2h), B_s(2h+1), B_s(2h+1))
-    __device__ float4 Bs(int t, int h) const {
-        return *reinterpret_cast<const float4 *>(B + t * G::DUP_STEP + h * 4 * G::TAUS * NQ);
+    static __device__ DupV<G::SPT> dupv(const float *p) {
+        const float4 *v = reinterpret_cast<const float4 *>(p);
+        if constexpr (G::SPT == 4) return {v[0], v[G::TAUS * G::NQ]};
+        else return {v[0]};
     }
-    __device__ float4 Cs(int t, int h) const {
-        return *reinterpret_cast<const float4 *>(C + t * G::DUP_STEP + h * 4 * G::TAUS * NQ);
-    }
+    __device__ DupV<G::SPT> Bs(int t) const { return dupv(B + t * G::DUP_STEP); }
+    __device__ DupV<G::SPT> Cs(int t) const { return dupv(C + t * G::DUP_STEP); }
     // the chunk's entry state from the checkpoint slab
-    __device__ void entry(St8 &h, const CpLane<NQ> &L) const {
+    __device__ void entry(St<G::SPT> &h, const CpLane<G> &L) const {
         const float *r0 = ck + (2 * L.pr) * G::NP, *r1 = r0 + G::NP;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) h.v[m] = f2(r0[L.state(m)], r1[L.state(m)]);
+        for (int m = 0; m < G::SPT; ++m) h.v[m] = f2(r0[L.state(m)], r1[L.state(m)]);
     }
 };
 
-__device__ __forceinline__ float2 dup_of(const float4 &lo4, const float4 &hi4, int m) {
-    return m == 0 ? lo(lo4) : m == 1 ? hi(lo4) : m == 2 ? lo(hi4) : hi(hi4);
-}
-
 // h <- one step; the step's dA returned in dA.
-template <typename E, int NQ>
-__device__ __forceinline__ void cp_advance(St8 &h, St8 &dA, const CpView<E, NQ> &v, const CpLane<NQ> &L,
-                                           int t) {
+template <typename E, typename G>
+__device__ __forceinline__ void cp_advance(St<G::SPT> &h, St<G::SPT> &dA, const CpView<E, G> &v,
+                                           const CpLane<G> &L, int t) {
     const float2 dt2 = v.dts(t);
     const float2 bx2 = mul2(dt2, v.xs(t));
-    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
+    const DupV<G::SPT> Bv = v.Bs(t);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < G::SPT; ++m) {
         dA.v[m] = ex2x2(mul2(dt2, L.nan[m]));
-        h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, dup_of(B0, B1, m)));
+        h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, Bv[m]));
     }
 }
 
 // h <- one step with a known dA (no ex2).
-template <typename E, int NQ>
-__device__ __forceinline__ void cp_replay(St8 &h, const St8 &dA, const CpView<E, NQ> &v, int t) {
+template <typename E, typename G>
+__device__ __forceinline__ void cp_replay(St<G::SPT> &h, const St<G::SPT> &dA, const CpView<E, G> &v, int t) {
     const float2 bx2 = mul2(v.dts(t), v.xs(t));
-    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1);
+    const DupV<G::SPT> Bv = v.Bs(t);
 #pragma unroll
-    for (int m = 0; m < 4; ++m) h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, dup_of(B0, B1, m)));
+    for (int m = 0; m < G::SPT; ++m) h.v[m] = fma2(dA.v[m], h.v[m], mul2(bx2, Bv[m]));
 }
 
 // One backward step t: hc = h_t, hp = h_{t-1}, dA = dA_t; r carries
 // dA_{t+1}*g_{t+1} in and dA_t*g_t out.
-template <typename E, int NQ, bool PROJ>
-__device__ __forceinline__ void cp_walk_step(const CpView<E, NQ> &v, const CpLane<NQ> &L, const St8 &hc,
-                                             const St8 &hp, const St8 &dA, St8 &r, St8 &dac, int t,
-                                             int nv, E *outp, int D, float *sd, int warp,
+template <typename E, typename G, bool PROJ>
+__device__ __forceinline__ void cp_walk_step(const CpView<E, G> &v, const CpLane<G> &L,
+                                             const St<G::SPT> &hc, const St<G::SPT> &hp,
+                                             const St<G::SPT> &dA, St<G::SPT> &r, St<G::SPT> &dac,
+                                             int t, int nv, E *outp, int D, float *sd, int warp,
                                              const Proj &pj)
 {
-    using G = CpGeo<NQ>;
+    constexpr int SPT = G::SPT, NQ = G::NQ;
     const float2 dt2 = v.dts(t), x2 = v.xs(t), dy2 = v.dys(t);
     const float2 bx2 = mul2(dt2, x2);
-    const float4 B0 = v.Bs(t, 0), B1 = v.Bs(t, 1), C0 = v.Cs(t, 0), C1 = v.Cs(t, 1);
-    float2 sB, sA, P[4];                  // P[m] = (sum over the pair of g*dt*x, of dy*h_t)
+    const DupV<SPT> Bv = v.Bs(t), Cv = v.Cs(t);
+    float2 sB, sA, P[SPT];                // P[m] = (sum over the pair of g*dt*x, of dy*h_t)
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-        const float2 g = fma2(dy2, dup_of(C0, C1, m), r.v[m]);
+    for (int m = 0; m < SPT; ++m) {
+        const float2 g = fma2(dy2, Cv[m], r.v[m]);
         const float2 rn = mul2(dA.v[m], g);
         const float2 u = mul2(rn, hp.v[m]);
-        sB = m ? fma2(g, dup_of(B0, B1, m), sB) : mul2(g, dup_of(B0, B1, m));
+        sB = m ? fma2(g, Bv[m], sB) : mul2(g, Bv[m]);
         sA = m ? fma2(L.nan[m], u, sA) : mul2(L.nan[m], u);
         dac.v[m] = fma2(dt2, u, dac.v[m]);
         const float2 pb = mul2(g, bx2), pc = mul2(dy2, hc.v[m]);
@@ -288,21 +303,27 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E, NQ> &v, const CpLan
         }
         if (t < nv && (NQ == 4 || L.q < 4) && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
     }
-    // dB | dC over the warp's channel pairs: lane bit 4 (and 3 for NQ <= 8)
-    // select-free, then lane bit 2 by kind for NQ = 4
-    P[0] = add2(P[0], shfl2(P[2], 16));
-    P[1] = add2(P[1], shfl2(P[3], 16));
-    float *row = sd + (t * CP_WARPS + warp) * 2 * G::NP;
-    if constexpr (NQ <= 8) P[0] = add2(P[0], shfl2(P[1], 8));
-    if constexpr (NQ == 4) {
-        const int kb = (L.lane >> 2) & 1;
+    // dB | dC over the warp's channel pairs: the pair bits among lane bits 4
+    // and 3 select-free (the states' order tau), the lowest pair bit by kind
+    // where one is left
+    float *row = sd + (t * G::WARPS + warp) * 2 * G::NP;
+    if constexpr (SPT == 4) {
+        P[0] = add2(P[0], shfl2(P[2], 16));
+        P[1] = add2(P[1], shfl2(P[3], 16));
+        if constexpr (NQ <= 8) P[0] = add2(P[0], shfl2(P[1], 8));
+    } else {
+        P[0] = add2(P[0], shfl2(P[1], 16));
+    }
+    constexpr int KIND_BIT = SPT == 4 && NQ == 4 ? 2 : SPT == 2 && NQ == 8 ? 3 : -1;
+    if constexpr (KIND_BIT >= 0) {
+        const int kb = (L.lane >> KIND_BIT) & 1;
         float kk = kb ? P[0].y : P[0].x;
-        kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 4);
+        kk += __shfl_xor_sync(0xffffffffu, kb ? P[0].x : P[0].y, 1 << KIND_BIT);
         row[kb * G::NP + L.state(0)] = kk;
     } else {
         row[L.state(0)] = P[0].x;
         row[G::NP + L.state(0)] = P[0].y;
-        if constexpr (NQ == 16) {
+        if constexpr (SPT == 4 && NQ == 16) {
             row[L.state(1)] = P[1].x;
             row[G::NP + L.state(1)] = P[1].y;
         }
@@ -311,19 +332,20 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E, NQ> &v, const CpLan
 
 // The state entering sub-chunk j of a chunk: the checkpoint slab (j == 0) or
 // the pre-pass slot (j > 0).
-template <typename E, int NQ>
-__device__ __forceinline__ void cp_entry(St8 &h, const CpView<E, NQ> &v, const CpLane<NQ> &L, int j,
+template <typename E, typename G>
+__device__ __forceinline__ void cp_entry(St<G::SPT> &h, const CpView<E, G> &v, const CpLane<G> &L, int j,
                                          const float *slot_in)
 {
     if (j == 0) {
         v.entry(h, L);
     } else {
-        const float4 a0 = reinterpret_cast<const float4 *>(slot_in)[0];
-        const float4 a1 = reinterpret_cast<const float4 *>(slot_in)[1];
-        h.v[0] = lo(a0);
-        h.v[1] = hi(a0);
-        h.v[2] = lo(a1);
-        h.v[3] = hi(a1);
+        const float4 *sl = reinterpret_cast<const float4 *>(slot_in);
+#pragma unroll
+        for (int k = 0; k < G::SPT / 2; ++k) {
+            const float4 a = sl[k];
+            h.v[2 * k] = lo(a);
+            h.v[2 * k + 1] = hi(a);
+        }
     }
 }
 
@@ -331,35 +353,36 @@ __device__ __forceinline__ void cp_entry(St8 &h, const CpView<E, NQ> &v, const C
 // carry r. All 8 decays are kept; of the states only h_4..h_7, and h_{-1}..h_3
 // are recomputed from the entry state with the kept decays (no ex2) when the
 // walk reaches them, which keeps the live registers low.
-template <typename E, int NQ, bool PROJ>
-__device__ __forceinline__ void cp_walk(const CpView<E, NQ> &v, const CpLane<NQ> &L, int j,
-                                        const float *slot_in, St8 &r, St8 &dac, int nv, E *outp,
-                                        int D, float *sd, int warp, const Proj &pj)
+template <typename E, typename G, bool PROJ>
+__device__ __forceinline__ void cp_walk(const CpView<E, G> &v, const CpLane<G> &L, int j,
+                                        const float *slot_in, St<G::SPT> &r, St<G::SPT> &dac, int nv,
+                                        E *outp, int D, float *sd, int warp, const Proj &pj)
 {
-    St8 dA[CP_SUB], hk[4];                // hk[t - 4] = h_t
+    using S = St<G::SPT>;
+    S dA[CP_SUB], hk[4];                  // hk[t - 4] = h_t
     {
-        St8 h;
-        cp_entry<E, NQ>(h, v, L, j, slot_in);
+        S h;
+        cp_entry<E, G>(h, v, L, j, slot_in);
 #pragma unroll
         for (int t = 0; t < CP_SUB; ++t) {
-            cp_advance<E, NQ>(h, dA[t], v, L, t);
+            cp_advance<E, G>(h, dA[t], v, L, t);
             if (t >= 4) hk[t - 4] = h;
         }
     }
 #pragma unroll
     for (int t = CP_SUB - 1; t >= 5; --t)
-        cp_walk_step<E, NQ, PROJ>(v, L, hk[t - 4], hk[t - 5], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
-    St8 hl[5];                            // hl[t + 1] = h_t for t = -1 .. 3
-    cp_entry<E, NQ>(hl[0], v, L, j, slot_in);
+        cp_walk_step<E, G, PROJ>(v, L, hk[t - 4], hk[t - 5], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+    S hl[5];                              // hl[t + 1] = h_t for t = -1 .. 3
+    cp_entry<E, G>(hl[0], v, L, j, slot_in);
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         hl[t + 1] = hl[t];
-        cp_replay<E, NQ>(hl[t + 1], dA[t], v, t);
+        cp_replay<E, G>(hl[t + 1], dA[t], v, t);
     }
-    cp_walk_step<E, NQ, PROJ>(v, L, hk[0], hl[4], dA[4], r, dac, 4, nv, outp, D, sd, warp, pj);
+    cp_walk_step<E, G, PROJ>(v, L, hk[0], hl[4], dA[4], r, dac, 4, nv, outp, D, sd, warp, pj);
 #pragma unroll
     for (int t = 3; t >= 0; --t)
-        cp_walk_step<E, NQ, PROJ>(v, L, hl[t + 1], hl[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
+        cp_walk_step<E, G, PROJ>(v, L, hl[t + 1], hl[t], dA[t], r, dac, t, nv, outp, D, sd, warp, pj);
 }
 
 // The item sequence of one CTA: chunks chi down to clo; in a chunk with mv
@@ -382,8 +405,8 @@ struct CpCursor {
     }
 };
 
-template <typename E, int NQ, bool PROJ>
-__global__ void __launch_bounds__(CP_THREADS, MMS_BWD_CP_MINB)
+template <typename E, typename G, bool PROJ>
+__global__ void __launch_bounds__(G::THREADS, 2)
 bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict__ ddt,
               float *__restrict__ part_bc, float *__restrict__ part_a,
               const float *__restrict__ seg_e, int T, int D, int N, int M, int nblk, int cps,
@@ -391,16 +414,17 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 {
     Proj pj = pj_in;
     pj.on = PROJ;
-    using G = CpGeo<NQ>;
-    using Q = CpTile<E, NQ>;
+    constexpr int SPT = G::SPT, NQ = G::NQ, THREADS = G::THREADS;
+    using Q = CpTile<E, G>;
+    using S = St<SPT>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;                                  // [CP_NAT][Q::F]
     float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (G::DUP)
-    float *sd = dup + G::DUP;                              // [8][4 warps][2 NP]
-    float *slots = sd + G::SD;                             // [M-1][128][8]
-    const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * CpSmem::SLOT);
+    float *sd = dup + G::DUP;                              // [8][WARPS][2 NP]
+    float *slots = sd + G::SD;                             // [M-1][THREADS][2 SPT]
+    const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * G::SLOT);
 
-    const CpLane<NQ> L(aneg, D, N, PROJ);
+    const CpLane<G> L(aneg, D, N, PROJ);
     const int tid = threadIdx.x, brow = blockIdx.y;
     const int K = M * CP_SUB;
     const int nchunk = (T + K - 1) / K;
@@ -428,13 +452,13 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         tma4(dst + 4 * Q::CK, &maps.ck, 0, d0, at.c - 1, brow, bar);
     };
 
-    St8 r, dac;
+    S r, dac;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) r.v[m] = dac.v[m] = f2(0.f, 0.f);
+    for (int m = 0; m < SPT; ++m) r.v[m] = dac.v[m] = f2(0.f, 0.f);
     if (sg + 1 < nsg) {                                    // adjoint carry from the later segments
         const float *src = seg_e + ((size_t)brow * nsg + sg) * plane + (size_t)L.d0c * N;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < SPT; ++m) {
             const int s = L.state(m);
             r.v[m] = f2(L.dv0 && s < N ? src[s] : 0.f, L.dv1 && s < N ? src[N + s] : 0.f);
         }
@@ -452,8 +476,8 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     __syncthreads();
 
     // this thread's share of the dB|dC flush: rows fr, fr + RPP, ... of a
-    // walked sub-chunk, column fj of the four warps' sums
-    constexpr int COLS = 2 * G::NP, RPP = CP_THREADS / COLS;
+    // walked sub-chunk, column fj of the warps' sums
+    constexpr int COLS = 2 * G::NP, RPP = THREADS / COLS;
     const int fr = tid / COLS, fj = tid % COLS;
     const bool fvalid = fj % G::NP < N;
     float *pbc_col = pbc + (fj / G::NP) * N + fj % G::NP;
@@ -462,18 +486,21 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         for (int h = 0; h < CP_SUB / RPP; ++h) {
             const int i = fr + RPP * h;
             if (i < nvp && fvalid) {
-                const float *q = sd + i * CP_WARPS * COLS + fj;
-                pbc_col[(size_t)(t0p + i) * 2 * N] = (q[0] + q[COLS]) + (q[2 * COLS] + q[3 * COLS]);
+                const float *q = sd + i * G::WARPS * COLS + fj;
+                float a = q[0] + q[COLS];
+#pragma unroll
+                for (int w = 2; w < G::WARPS; w += 2) a += q[w * COLS] + q[(w + 1) * COLS];
+                pbc_col[(size_t)(t0p + i) * 2 * N] = a;
             }
         }
     };
     // this thread's share of the B, C duplication: combination pc = (half,
     // order, quad) of a step, rows pat, pat + GRP, ... of the 16 (array, step) rows
-    constexpr int CMB = 2 * G::TAUS * NQ, GRP = CP_THREADS / CMB;
+    constexpr int CMB = G::HALVES * G::TAUS * NQ, GRP = THREADS / CMB;
     const int pc = tid % CMB, pat = tid / CMB;
     const int pq = pc % NQ, pti = (pc / NQ) % G::TAUS, ph = pc / (NQ * G::TAUS);
-    const int ptau = NQ == 16 ? pti << 1 : pti;
-    const int ps0 = 4 * pq + ((2 * ph) ^ ptau), ps1 = 4 * pq + ((2 * ph + 1) ^ ptau);
+    const int ptau = SPT == 4 && NQ == 16 ? pti << 1 : pti;
+    const int ps0 = SPT * pq + ((2 * ph) ^ ptau), ps1 = SPT * pq + ((2 * ph + 1) ^ ptau);
 
     CpCursor cur(chi, M, T, K, nchunk);
     int pend_t0 = -1, pend_nv = 0;
@@ -507,7 +534,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         }
         if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
             float *dts = st + Q::ARR;
-            for (int e = tid; e < CP_SUB * G::DPB; e += CP_THREADS)
+            for (int e = tid; e < CP_SUB * G::DPB; e += THREADS)
                 dts[e] = fmaf(pj.range, sigmoid_fast(dts[e]), pj.lo);
         }
         if (tid == 0 && i + 2 < total) {
@@ -517,24 +544,25 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         }
         __syncthreads();
 
-        const CpView<E, NQ> v(st, dup, L);
+        const CpView<E, G> v(st, dup, L);
         const int u = c * M + j;                           // sub-chunk index in the sequence
         const int t0 = u * CP_SUB;
         const int nv = min(CP_SUB, T - t0);
-        const float *slot_in = slots + (size_t)(j - 1) * CpSmem::SLOT + tid * 8;
+        const float *slot_in = slots + (size_t)(j - 1) * G::SLOT + tid * 2 * SPT;
         if (!walk) {
             // pre-pass: the state entering sub-chunk j+1 into slot j
-            St8 h, dA;
-            cp_entry<E, NQ>(h, v, L, j, slot_in);
+            S h, dA;
+            cp_entry<E, G>(h, v, L, j, slot_in);
 #pragma unroll
-            for (int t = 0; t < CP_SUB; ++t) cp_advance<E, NQ>(h, dA, v, L, t);
-            float4 *sl = reinterpret_cast<float4 *>(slots + (size_t)j * CpSmem::SLOT + tid * 8);
-            sl[0] = make_float4(h.v[0].x, h.v[0].y, h.v[1].x, h.v[1].y);
-            sl[1] = make_float4(h.v[2].x, h.v[2].y, h.v[3].x, h.v[3].y);
+            for (int t = 0; t < CP_SUB; ++t) cp_advance<E, G>(h, dA, v, L, t);
+            float4 *sl = reinterpret_cast<float4 *>(slots + (size_t)j * G::SLOT + tid * 2 * SPT);
+#pragma unroll
+            for (int k = 0; k < SPT / 2; ++k)
+                sl[k] = make_float4(h.v[2 * k].x, h.v[2 * k].y, h.v[2 * k + 1].x, h.v[2 * k + 1].y);
         } else {
             // this lane's output after the dx / ddt exchange: array (lane bit 1), channel (bit 0)
             E *outp = ((L.lane >> 1) & 1 ? ddt : dx) + rowD + (size_t)t0 * D + L.d0c + (L.lane & 1);
-            cp_walk<E, NQ, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
+            cp_walk<E, G, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
             pend_t0 = t0;
             pend_nv = nv;
         }
@@ -548,7 +576,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     if (pend_t0 >= 0) flush(pend_t0, pend_nv);
     float *pa = part_a + ((size_t)brow * nsg + sg) * plane + (size_t)L.d0c * N;
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
+    for (int m = 0; m < SPT; ++m) {
         const int s = L.state(m);
         if (s < N) {
             if (L.dv0) pa[s] = -dac.v[m].x;
@@ -557,10 +585,9 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     }
 }
 
-template <int NQ>
+template <typename G>
 bool build_cp_maps(const BwdArgs &a, CpMaps *m)
 {
-    using G = CpGeo<NQ>;
     const auto fn = tma_encoder();
     if (!fn || !tma_context()) return false;
     const cuuint64_t dX[3] = {(cuuint64_t)a.D, (cuuint64_t)a.T, (cuuint64_t)a.Bt};
@@ -576,33 +603,33 @@ bool build_cp_maps(const BwdArgs &a, CpMaps *m)
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
-template <typename E, int NQ, bool PROJ>
+template <typename E, typename G, bool PROJ>
 cudaError_t launch_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                       int nblk, SegPlan sp, cudaStream_t stream)
 {
+    using Q = CpTile<E, G>;
     CpMaps maps;
     memset(&maps, 0, sizeof(maps));
-    if (!build_cp_maps<NQ>(a, &maps)) return cudaErrorInvalidValue;
+    if (!build_cp_maps<G>(a, &maps)) return cudaErrorInvalidValue;
     const int M = a.K / CP_SUB;
-    const size_t smem = CpSmem::bytes<E, NQ>(CP_MAXM);     // one opt-in size for every M
-    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, NQ, PROJ>>(smem);
+    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, G, PROJ>>(Q::smem(CP_MAXM));   // one size for every M
     if (e != cudaSuccess) return e;
     const uint32_t limit = tma_wait_limit();
     const int skip = tma_skip_item();
-    dim3 grid((a.D + CpGeo<NQ>::DPB - 1) / CpGeo<NQ>::DPB, a.Bt, sp.S);
-    bwd_kernel_cp<E, NQ, PROJ><<<grid, CP_THREADS, CpSmem::bytes<E, NQ>(M), stream>>>(
+    dim3 grid((a.D + G::DPB - 1) / G::DPB, a.Bt, sp.S);
+    bwd_kernel_cp<E, G, PROJ><<<grid, G::THREADS, Q::smem(M), stream>>>(
         a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,
         a.T, a.D, a.N, M, nblk, sp.cps, maps, a.proj, limit, skip);
     return cudaGetLastError();
 }
 
-template <int NQ>
-cudaError_t launch_cp_n(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+template <typename G>
+cudaError_t launch_cp_g(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                         int nblk, SegPlan sp, cudaStream_t stream)
 {
-    if (a.bf16) return launch_cp<__nv_bfloat16, NQ, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    return a.proj.on ? launch_cp<float, NQ, true>(a, part_bc, part_a, seg_e, nblk, sp, stream)
-                     : launch_cp<float, NQ, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    if (a.bf16) return launch_cp<__nv_bfloat16, G, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    return a.proj.on ? launch_cp<float, G, true>(a, part_bc, part_a, seg_e, nblk, sp, stream)
+                     : launch_cp<float, G, false>(a, part_bc, part_a, seg_e, nblk, sp, stream);
 }
 
 }  // namespace
@@ -610,10 +637,8 @@ cudaError_t launch_cp_n(const BwdArgs &a, float *part_bc, float *part_a, const f
 bool bwd_cp_applies(const BwdArgs &a)
 {
     if (!cp_shape(a.N, a.K)) return false;
-    // stride 8 at 8 < N <= 16 runs the 8-state kernel (mms_bwd_w8.cu), bf16
-    // always and fp32 unless MMS_BWD_CP_K8: bf16 and fp32 run the same kernel
-    // on a shape, so bf16 storage only rounds the fp32 results
-    if (w8_shape(a.N, a.K) && (!MMS_BWD_CP_K8 || a.bf16)) return false;
+    // bf16 and fp32 run the same kernel on a shape, so bf16 storage only
+    // rounds the fp32 results
     if (a.bf16 && (a.D % 8 != 0 || a.proj.on)) return false;
     return vec_ok(a.D, a.x, a.dt, a.dy);
 }
@@ -621,10 +646,20 @@ bool bwd_cp_applies(const BwdArgs &a)
 cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                           int nblk, SegPlan sp, cudaStream_t stream)
 {
-    switch (groups_for(a.N)) {
-    case 4: return launch_cp_n<4>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    case 8: return launch_cp_n<8>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    case 16: return launch_cp_n<16>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    const int G = groups_for(a.N);
+#if MMS_BWD_CP2_MAXN > 0
+    if (cp_two_states(a.N)) {
+        switch (G) {
+        case 4: return launch_cp_g<CpGeo<8, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+        case 8: return launch_cp_g<CpGeo<16, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+        default: return cudaErrorInvalidValue;
+        }
+    }
+#endif
+    switch (G) {
+    case 4: return launch_cp_g<CpGeo<4, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 8: return launch_cp_g<CpGeo<8, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 16: return launch_cp_g<CpGeo<16, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -88,11 +88,23 @@ struct SegPlan {
     int cps;    // checkpoint chunks per segment
 };
 
+// Stride 8 at 8 < N <= 16 on the channel-pair backward instead of the
+// 8-state one.
+#ifndef MMS_BWD_CP_K8
+#define MMS_BWD_CP_K8 0
+#endif
+// The channel-pair backward with 2 states per thread (256-thread CTAs) up to
+// this N (at most 32), else 4 states per thread (128-thread CTAs).
+#ifndef MMS_BWD_CP2_MAXN
+#define MMS_BWD_CP2_MAXN 0
+#endif
+
 // The shapes of the 8-state backward (mms_bwd_w8.cu): 8 < N <= 16, K == 8.
-inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8; }
+inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8 && !MMS_BWD_CP_K8; }
 // The shapes of the channel-pair backward (mms_bwd_cp.cu): 8 < N <= 64,
-// K a multiple of 8 up to 64.
-inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64; }
+// K a multiple of 8 up to 64, except the 8-state kernel's.
+inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64 && !w8_shape(N, K); }
+inline bool cp_two_states(int N) { return N <= MMS_BWD_CP2_MAXN && N <= 32; }
 
 // Bounded waits of the TMA-staged kernels: polls of one stage's completion
 // barrier before a kernel gives up (default 2^22), and a staged item whose

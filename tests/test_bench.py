@@ -40,3 +40,17 @@ def test_step_bytes_match_the_roofline_units(bench):
 ])
 def test_launch_count_follows_the_dispatch_rules(bench, shape, launches):
     assert bench.launches_per_step(*shape) == launches
+
+
+# (N, K, D)
+@pytest.mark.parametrize("shape,kernel", [
+    ((16, 8, 2304), "bwd_kernel_w8"),       # config 1
+    ((64, 8, 2048), "bwd_kernel_cp"),       # config 3b
+    ((16, 64, 2304), "bwd_kernel_cp"),      # config 1 at the reference's stride
+    ((8, 8, 2304), "bwd_kernel_k8"),        # d_state 8
+    ((16, 100, 2304), "bwd_kernel"),        # stride beyond 64
+    ((32, 16, 2303), "bwd_kernel"),         # unaligned channel count
+])
+def test_roofline_names_the_backward_kernel_the_library_runs(bench, shape, kernel):
+    n, k, d = shape
+    assert bench.bwd_kernel_label(n, k, d) == f"mms_bwd ({kernel} + reduce_kernel)"
