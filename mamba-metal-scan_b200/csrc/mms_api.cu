@@ -128,7 +128,7 @@ const char *mms_status_string(int status)
 int mms_fwd(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
             float *y, float *ckpt, int Bt, int T, int D, int N, int K, void *stream)
 {
-    return fwd_impl(x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f});
+    return fwd_impl(x, dt, aneg, B, C, y, ckpt, Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f, 0.f});
 }
 
 int mms_fwd_proj(const float *x, const float *dt_logit, const float *a_param, const float *B,
@@ -137,7 +137,7 @@ int mms_fwd_proj(const float *x, const float *dt_logit, const float *a_param, co
 {
     if (!proj_ok(dt_min, dt_max)) return MMS_ERR_INVALID_ARG;
     return fwd_impl(x, dt_logit, a_param, B, C, y, ckpt, Bt, T, D, N, K, stream,
-                    mms::Proj{1, dt_min, dt_max - dt_min});
+                    mms::Proj{1, dt_min, dt_max - dt_min, 1.f / (dt_max - dt_min)});
 }
 
 size_t mms_bwd_workspace_size(int Bt, int T, int D, int N, int K)
@@ -152,7 +152,7 @@ int mms_bwd(const float *x, const float *dt, const float *aneg, const float *B, 
             void *stream)
 {
     return bwd_impl(x, dt, aneg, B, C, dy, ckpt, dx, ddt, daneg, dB, dC, workspace, workspace_bytes,
-                    Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f});
+                    Bt, T, D, N, K, stream, mms::Proj{0, 0.f, 0.f, 0.f});
 }
 
 int mms_bwd_proj(const float *x, const float *dt_logit, const float *a_param, const float *B,
@@ -164,7 +164,7 @@ int mms_bwd_proj(const float *x, const float *dt_logit, const float *a_param, co
     if (!proj_ok(dt_min, dt_max)) return MMS_ERR_INVALID_ARG;
     return bwd_impl(x, dt_logit, a_param, B, C, dy, ckpt, dx, d_dt_logit, d_a_param, dB, dC,
                     workspace, workspace_bytes, Bt, T, D, N, K, stream,
-                    mms::Proj{1, dt_min, dt_max - dt_min});
+                    mms::Proj{1, dt_min, dt_max - dt_min, 1.f / (dt_max - dt_min)});
 }
 
 int mms_step(const float *x, const float *dt, const float *aneg, const float *B, const float *C,
@@ -226,7 +226,7 @@ int mms_fwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
     if (!aligned(aneg, 16) || !aligned(B, 16) || !aligned(C, 16) || !aligned(ckpt, 16) ||
         !aligned(x, 16) || !aligned(dt, 16) || !aligned(y, 16))
         return MMS_ERR_MISALIGNED;
-    mms::FwdArgs a{fp(x), fp(dt), aneg, B, C, fp(y), ckpt, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
+    mms::FwdArgs a{fp(x), fp(dt), aneg, B, C, fp(y), ckpt, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f, 0.f}, 1};
     return status_of(mms::launch_fwd(a, static_cast<cudaStream_t>(stream)));
 }
 
@@ -248,7 +248,7 @@ int mms_bwd_bf16(const uint16_t *x, const uint16_t *dt, const float *aneg, const
     if (!workspace || workspace_bytes < need) return MMS_ERR_WORKSPACE;
     if (!aligned(workspace, 256)) return MMS_ERR_MISALIGNED;
     mms::BwdArgs a{fp(x), fp(dt), aneg, B, C, fp(dy), ckpt, fp(dx), fp(ddt), daneg, dB, dC,
-                   workspace, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f}, 1};
+                   workspace, Bt, T, D, N, K, mms::Proj{0, 0.f, 0.f, 0.f}, 1};
     return status_of(mms::launch_bwd(a, static_cast<cudaStream_t>(stream)));
 }
 

@@ -373,10 +373,10 @@ __device__ __forceinline__ void walk_group(const TileView<G> &v, const float2 (&
                     int fn;
                     transposed_reduce<2, G / 2, 1>(vn, L.lane, fn);
                     // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
-                    if (pj.on && L.n_ddt) vn[0] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
+                    if (pj.on && L.n_ddt) vn[0] *= dt_slope(pj, dtv);
                     if (L.n_writer) outp[(size_t)i * D] = from_f<E>(vn[0]);
                 } else if (L.n_writer) {
-                    if (pj.on) vn[1] *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
+                    if (pj.on) vn[1] *= dt_slope(pj, dtv);
                     dxo[(size_t)i * D] = from_f<E>(vn[0]);
                     ddto[(size_t)i * D] = from_f<E>(vn[1]);
                 }

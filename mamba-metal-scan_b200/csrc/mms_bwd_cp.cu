@@ -299,7 +299,7 @@ __device__ __forceinline__ void cp_walk_step(const CpView<E, G> &v, const CpLane
         // its own output array and channel; lanes with q < 4 store
         if (PROJ && b1) {
             const float dtv = b0 ? dt2.y : dt2.x;
-            kv *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
+            kv *= dt_slope(pj, dtv);
         }
         if (t < nv && (NQ == 4 || L.q < 4) && (b0 ? L.dv1 : L.dv0)) outp[(size_t)t * D] = from_f<E>(kv);
     }

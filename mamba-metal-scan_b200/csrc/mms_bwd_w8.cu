@@ -283,7 +283,7 @@ __device__ __forceinline__ void w8_walk(const W8View &v, const float2 (&hb)[4], 
             float keep = L.h ? v1 : v0;
             keep += __shfl_xor_sync(0xffffffffu, L.h ? v0 : v1, 1);
             // prologue: d(logit) = ddt * d dt / d logit = ddt * (dt-lo)(lo+range-dt)/range
-            if (pj.on && L.h) keep *= (dtv - pj.lo) * (pj.lo + pj.range - dtv) / pj.range;
+            if (pj.on && L.h) keep *= dt_slope(pj, dtv);
             if (L.dval) outq[(size_t)k * D] = from_f<E>(keep);
         }
         // dB|dC over the warp's 16 channels

@@ -53,8 +53,12 @@ __device__ __forceinline__ float ex2_poly(float x) {
 }
 
 // sigmoid(z) = 1 / (1 + 2^(-z*log2 e)); saturates to 0 / 1 for large |z|.
+// The reciprocal is MUFU's (rcp.approx, about 1 ulp; 1/inf = 0, so a large
+// negative z gives 0).
 __device__ __forceinline__ float sigmoid_fast(float z) {
-    return __frcp_rn(1.f + ex2(-z * MMS_LOG2E));
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + ex2(-z * MMS_LOG2E)));
+    return r;
 }
 
 // softplus(a) = log(1 + e^a), = a once e^a dwarfs 1 in fp32.

@@ -63,6 +63,7 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
 {
     Proj pj = pj_in;                 // the prologue is compiled in only where it is used
     pj.on = PROJ;
+    static_assert(!PROJ || sizeof(E) == 4, "the prologue takes fp32 arrays");
     using S = FwdShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = S::TT, ROWF = S::ROWF;
     constexpr int CHF = TileRow<2, DPB, E>::CHF;           // floats of x, dt per staged step
@@ -131,16 +132,24 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
                 min(TT, te - tb - kn * TT), d0, D, N, tid);
         cp_commit();
 
-        const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
+        float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
         const int t0 = tb + k * TT;
+        if constexpr (PROJ) {
+            // dt from its logit once per element: the channel's G lanes (one
+            // warp) share its column of the tile
+            for (int j = g; j < TT; j += G) {
+                float *p = tile + j * RROW + DPB + c;
+                *p = fmaf(pj.range, sigmoid_fast(*p), pj.lo);
+            }
+            __syncwarp();
+        }
 #pragma unroll
         for (int j = 0; j < TT; ++j) {
             const float *row = tile + j * RROW;
             const E *re = reinterpret_cast<const E *>(row);
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
             const float xv = to_f(re[c]);
-            float dtv = to_f(re[DPB + c]);
-            if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
+            const float dtv = to_f(re[DPB + c]);
             const float4 Bv = *reinterpret_cast<const float4 *>(row + CHF + 4 * g);
             const float4 Cv = *reinterpret_cast<const float4 *>(row + CHF + NPAD + 4 * g);
             const float bx = dtv * xv;

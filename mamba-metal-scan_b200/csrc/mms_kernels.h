@@ -17,7 +17,14 @@ namespace mms {
 struct Proj {
     int on;
     float lo, range;
+    float inv_range;            // 1 / range
 };
+
+// The prologue's d dt / d logit = range * s * (1 - s) with s the sigmoid,
+// written from dt = lo + range * s.
+__device__ __forceinline__ float dt_slope(const Proj &pj, float dtv) {
+    return (dtv - pj.lo) * (pj.lo + pj.range - dtv) * pj.inv_range;
+}
 
 // bf16 != 0: the (B, T, D) channel arrays (x, dt, y; dy, dx, ddt) hold bf16
 // values (the pointers are passed through as float * and reinterpreted by

@@ -64,6 +64,7 @@ seg_local_kernel(const E *__restrict__ u, const E *__restrict__ dt,
 {
     Proj pj = pj_in;                 // the prologue is compiled in only where it is used
     pj.on = PROJ;
+    static_assert(!PROJ || sizeof(E) == 4, "the prologue takes fp32 arrays");
     using S = SegLocalShape<G>;
     constexpr int DPB = S::DPB, NPAD = S::NPAD, TT = SEGL_TT;
     constexpr int CHF = TileRow<2, DPB, E>::CHF;           // floats of u, dt per step
@@ -113,18 +114,26 @@ seg_local_kernel(const E *__restrict__ u, const E *__restrict__ dt,
         const int kn = k + SEGL_STAGES - 1;
         if (kn < ntiles) stage(kn % SEGL_STAGES, kn);
         cp_commit();
-        const float *tile = smem + (k % SEGL_STAGES) * TT * ROWF;
+        float *tile = smem + (k % SEGL_STAGES) * TT * ROWF;
         const int tk = tstart(k);
+        if constexpr (PROJ) {
+            // dt from its logit once per element (the channel's G lanes, one
+            // warp, share its column); rows past the segment's end were staged
+            // as zeros and keep dt = 0 (dA = 1, no input) rather than mapped
+            for (int j = g; j < TT; j += G) {
+                float *p = tile + j * ROWF + DPB + c;
+                *p = tk + j < te ? fmaf(pj.range, sigmoid_fast(*p), pj.lo) : 0.f;
+            }
+            __syncwarp();
+        }
 #pragma unroll
         for (int jj = 0; jj < TT; ++jj) {
             // rows past the segment's end were staged as zeros: dA = 1, no input
-            // (with the prologue, dt = 0 must be kept there rather than mapped)
             const int j = BWD ? TT - 1 - jj : jj;
             const float *r = tile + j * ROWF;
             const E *re = reinterpret_cast<const E *>(r);
             const float uv = to_f(re[c]);
-            float dtv = to_f(re[DPB + c]);
-            if (pj.on) dtv = tk + j < te ? fmaf(pj.range, sigmoid_fast(dtv), pj.lo) : 0.f;
+            const float dtv = to_f(re[DPB + c]);
             const float4 R = *reinterpret_cast<const float4 *>(r + CHF + 4 * g);
             const float2 dt2 = f2(dtv, dtv);
             // a share of the exponentials on the FMA pipe (see MMS_SEGL_POLY)
