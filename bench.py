@@ -88,10 +88,10 @@ def launches_per_step(bt, t_len, d, n, k):
     g = 1
     while g < (n + 3) // 4:
         g *= 2
-    per_sm = 4 if (8 < n <= 16 and k == 8) else 2         # backward CTAs per SM
-    # the 8-state backward also splits below half a wave
-    split_b = _splits(bt, t_len, d, n, k, 256 // g, per_sm, 2 * N_SM if per_sm == 4 else N_SM)
-    split_g = _splits(bt, t_len, d, n, k, 256 // g, per_sm)  # the G-lane forward's plan
+    # the backward's plan: 2 CTAs per SM (channel-pair and G-lane kernels)
+    split_b = _splits(bt, t_len, d, n, k, 256 // g, 2)
+    # the G-lane forward's plan: 4 per SM at stride 8 and 8 < N <= 16
+    split_g = _splits(bt, t_len, d, n, k, 256 // g, 4 if (8 < n <= 16 and k == 8) else 2)
     if 8 < n <= 16 and bt * d >= N_SM * 128:
         split_f = False                                   # whole-state forward, no split
     elif 8 < n <= 16 and k >= 8 and d % 4 == 0 and split_g and _splits(bt, t_len, d, n, k, 128, 2):
@@ -103,10 +103,10 @@ def launches_per_step(bt, t_len, d, n, k):
 
 def bwd_kernel_label(n, k, d):
     """The backward kernel the library runs on (N, K, D) with aligned fp32 arrays."""
-    if 8 < n <= 16 and k == 8:
-        name = "bwd_kernel_w8"
-    elif 8 < n <= 64 and k % 8 == 0 and k <= 64 and d % 4 == 0:
+    if 8 < n <= 64 and k % 8 == 0 and k <= 64 and d % 4 == 0:
         name = "bwd_kernel_cp"
+    elif 8 < n <= 16 and k == 8:
+        name = "bwd_kernel_w8"                            # unaligned channel arrays
     else:
         name = "bwd_kernel_k8" if k == 8 else "bwd_kernel"
     return f"mms_bwd ({name} + reduce_kernel)"

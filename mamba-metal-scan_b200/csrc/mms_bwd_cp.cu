@@ -113,8 +113,9 @@ struct CpTile {
     static constexpr int CK = BC + 2 * CP_SUB * G::NP;
     static constexpr int F = CK + G::DPB * G::NP;
     static constexpr uint32_t BYTES = 4u * F;
-    static size_t smem(int m) {
-        return sizeof(float) * ((size_t)CP_NAT * F + G::DUP + G::SD + (size_t)(m - 1) * G::SLOT) + 64;
+    // `bufs`: 2 with one barrier per item (double-buffered rows and sums), else 1
+    static size_t smem(int m, int bufs) {
+        return sizeof(float) * ((size_t)CP_NAT * F + bufs * (G::DUP + G::SD) + (size_t)(m - 1) * G::SLOT) + 64;
     }
 };
 
@@ -405,7 +406,7 @@ struct CpCursor {
     }
 };
 
-template <typename E, typename G, bool PROJ>
+template <typename E, typename G, bool PROJ, bool ONEBAR>
 __global__ void __launch_bounds__(G::THREADS, 2)
 bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict__ ddt,
               float *__restrict__ part_bc, float *__restrict__ part_a,
@@ -419,9 +420,10 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     using S = St<SPT>;
     extern __shared__ __align__(128) float smem[];
     float *stages = smem;                                  // [CP_NAT][Q::F]
-    float *dup = stages + CP_NAT * Q::F;                   // B, C duplicated (G::DUP)
-    float *sd = dup + G::DUP;                              // [8][WARPS][2 NP]
-    float *slots = sd + G::SD;                             // [M-1][THREADS][2 SPT]
+    constexpr int BUFS = ONEBAR ? 2 : 1;
+    float *dup = stages + CP_NAT * Q::F;                   // [BUFS][G::DUP] B, C duplicated
+    float *sd = dup + BUFS * G::DUP;                       // [BUFS][8][WARPS][2 NP]
+    float *slots = sd + BUFS * G::SD;                      // [M-1][THREADS][2 SPT]
     const uint32_t bars = smem_u32(slots + (size_t)(M - 1) * G::SLOT);
 
     const CpLane<G> L(aneg, D, N, PROJ);
@@ -481,12 +483,12 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
     const int fr = tid / COLS, fj = tid % COLS;
     const bool fvalid = fj % G::NP < N;
     float *pbc_col = pbc + (fj / G::NP) * N + fj % G::NP;
-    auto flush = [&](int t0p, int nvp) {
+    auto flush = [&](const float *sdp, int t0p, int nvp) {
 #pragma unroll
         for (int h = 0; h < CP_SUB / RPP; ++h) {
             const int i = fr + RPP * h;
             if (i < nvp && fvalid) {
-                const float *q = sd + i * G::WARPS * COLS + fj;
+                const float *q = sdp + i * G::WARPS * COLS + fj;
                 float a = q[0] + q[COLS];
 #pragma unroll
                 for (int w = 2; w < G::WARPS; w += 2) a += q[w * COLS] + q[(w + 1) * COLS];
@@ -504,10 +506,37 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
 
     CpCursor cur(chi, M, T, K, nchunk);
     int pend_t0 = -1, pend_nv = 0;
+    const float *pend_sd = sd;
     int buf = 0;
     uint32_t parity = 0;
+    // ONEBAR: one barrier per item. The duplicated B / C rows and the
+    // per-warp dB|dC sums alternate between two buffers by item parity, so a
+    // thread can write item i's rows while others still read item i-1's, and
+    // flush item i-1's sums while others already walk item i; the barrier
+    // orders every buffer's reuse two items apart, and frees the stage of
+    // item i-1 for the copies of item i+2. Otherwise (one buffer each) a
+    // second barrier separates the rewrite and the flush from the walk.
+    auto prepare = [&](const float *st, float *dupi) {
+        // B, C of the 8 steps duplicated per state in the lane orders
+#pragma unroll
+        for (int k = 0; k < 2 * CP_SUB / GRP; ++k) {
+            const int at = pat + GRP * k;                  // array at / 8, step at % 8
+            const float *src = st + Q::BC + at * G::NP;
+            const float b0 = src[ps0], b1 = src[ps1];
+            *reinterpret_cast<float4 *>(dupi + at * G::DUP_STEP + 4 * pc) = make_float4(b0, b0, b1, b1);
+        }
+        if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
+            float *dts = const_cast<float *>(st) + Q::ARR;
+            for (int e = tid; e < CP_SUB * G::DPB; e += THREADS)
+                dts[e] = fmaf(pj.range, sigmoid_fast(dts[e]), pj.lo);
+        }
+    };
     for (int i = 0; i < total; ++i) {
         const bool ok = cp_wait_bar(bars + 8 * buf, parity, wait_limit);
+        float *st = stages + buf * Q::F;
+        const int par = ONEBAR ? (i & 1) : 0;
+        float *dupi = dup + par * G::DUP;
+        if (ONEBAR && ok) prepare(st, dupi);
         if (__syncthreads_or(!ok)) {
             // a stage never arrived: leave together, after the copies still in flight
             if (tid == 0) {
@@ -517,34 +546,23 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
             }
             return;
         }
-        const int c = cur.c, j = cur.j();
-        const bool walk = cur.walk();
-        float *st = stages + buf * Q::F;
-        if (pend_t0 >= 0) {
-            flush(pend_t0, pend_nv);
-            pend_t0 = -1;
-        }
-        // B, C of the 8 steps duplicated per state in the lane orders
-#pragma unroll
-        for (int k = 0; k < 2 * CP_SUB / GRP; ++k) {
-            const int at = pat + GRP * k;                  // array at / 8, step at % 8
-            const float *src = st + Q::BC + at * G::NP;
-            const float b0 = src[ps0], b1 = src[ps1];
-            *reinterpret_cast<float4 *>(dup + at * G::DUP_STEP + 4 * pc) = make_float4(b0, b0, b1, b1);
-        }
-        if constexpr (PROJ) {                              // dt from its logit, in place (fp32)
-            float *dts = st + Q::ARR;
-            for (int e = tid; e < CP_SUB * G::DPB; e += THREADS)
-                dts[e] = fmaf(pj.range, sigmoid_fast(dts[e]), pj.lo);
-        }
         if (tid == 0 && i + 2 < total) {
             fence_async_smem();                            // stage (i+2)%3 was read before the barrier
             issue(ahead, i + 2, buf == 0 ? 2 : buf - 1);
             ahead.next();
         }
-        __syncthreads();
+        if (pend_t0 >= 0) {
+            flush(pend_sd, pend_t0, pend_nv);
+            pend_t0 = -1;
+        }
+        if constexpr (!ONEBAR) {
+            prepare(st, dupi);
+            __syncthreads();
+        }
+        const int c = cur.c, j = cur.j();
+        const bool walk = cur.walk();
 
-        const CpView<E, G> v(st, dup, L);
+        const CpView<E, G> v(st, dupi, L);
         const int u = c * M + j;                           // sub-chunk index in the sequence
         const int t0 = u * CP_SUB;
         const int nv = min(CP_SUB, T - t0);
@@ -562,9 +580,11 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         } else {
             // this lane's output after the dx / ddt exchange: array (lane bit 1), channel (bit 0)
             E *outp = ((L.lane >> 1) & 1 ? ddt : dx) + rowD + (size_t)t0 * D + L.d0c + (L.lane & 1);
-            cp_walk<E, G, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sd, tid >> 5, pj);
+            float *sdi = sd + par * G::SD;
+            cp_walk<E, G, PROJ>(v, L, j, slot_in, r, dac, nv, outp, D, sdi, tid >> 5, pj);
             pend_t0 = t0;
             pend_nv = nv;
+            pend_sd = sdi;
         }
         cur.next();
         if (++buf == CP_NAT) {
@@ -573,7 +593,7 @@ bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict_
         }
     }
     __syncthreads();
-    if (pend_t0 >= 0) flush(pend_t0, pend_nv);
+    if (pend_t0 >= 0) flush(pend_sd, pend_t0, pend_nv);
     float *pa = part_a + ((size_t)brow * nsg + sg) * plane + (size_t)L.d0c * N;
 #pragma unroll
     for (int m = 0; m < SPT; ++m) {
@@ -603,24 +623,43 @@ bool build_cp_maps(const BwdArgs &a, CpMaps *m)
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
+// One barrier per item where the double buffers still leave 2 CTAs per SM
+// (228 KB of shared memory, 1 KB of it reserved per CTA), except at 8 lanes
+// per pair (d_state 20..32), which measured 1.5 % slower with it.
+template <typename E, typename G>
+bool cp_onebar(int M)
+{
+    return G::NQ != 8 && CpTile<E, G>::smem(M, 2) + 1024 <= 228 * 1024 / 2;
+}
+
+template <typename E, typename G, bool PROJ, bool ONEBAR>
+cudaError_t launch_cpb(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
+                       int nblk, SegPlan sp, const CpMaps &maps, cudaStream_t stream)
+{
+    using Q = CpTile<E, G>;
+    const int M = a.K / CP_SUB;
+    const int bufs = ONEBAR ? 2 : 1;
+    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, G, PROJ, ONEBAR>>(Q::smem(CP_MAXM, bufs));
+    if (e != cudaSuccess) return e;                        // one opt-in size for every M
+    const uint32_t limit = tma_wait_limit();
+    const int skip = tma_skip_item();
+    dim3 grid((a.D + G::DPB - 1) / G::DPB, a.Bt, sp.S);
+    bwd_kernel_cp<E, G, PROJ, ONEBAR><<<grid, G::THREADS, Q::smem(M, bufs), stream>>>(
+        a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,
+        a.T, a.D, a.N, M, nblk, sp.cps, maps, a.proj, limit, skip);
+    return cudaGetLastError();
+}
+
 template <typename E, typename G, bool PROJ>
 cudaError_t launch_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                       int nblk, SegPlan sp, cudaStream_t stream)
 {
-    using Q = CpTile<E, G>;
     CpMaps maps;
     memset(&maps, 0, sizeof(maps));
     if (!build_cp_maps<G>(a, &maps)) return cudaErrorInvalidValue;
-    const int M = a.K / CP_SUB;
-    cudaError_t e = smem_opt_in<bwd_kernel_cp<E, G, PROJ>>(Q::smem(CP_MAXM));   // one size for every M
-    if (e != cudaSuccess) return e;
-    const uint32_t limit = tma_wait_limit();
-    const int skip = tma_skip_item();
-    dim3 grid((a.D + G::DPB - 1) / G::DPB, a.Bt, sp.S);
-    bwd_kernel_cp<E, G, PROJ><<<grid, G::THREADS, Q::smem(M), stream>>>(
-        a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,
-        a.T, a.D, a.N, M, nblk, sp.cps, maps, a.proj, limit, skip);
-    return cudaGetLastError();
+    return cp_onebar<E, G>(a.K / CP_SUB)
+               ? launch_cpb<E, G, PROJ, true>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream)
+               : launch_cpb<E, G, PROJ, false>(a, part_bc, part_a, seg_e, nblk, sp, maps, stream);
 }
 
 template <typename G>
@@ -637,8 +676,8 @@ cudaError_t launch_cp_g(const BwdArgs &a, float *part_bc, float *part_a, const f
 bool bwd_cp_applies(const BwdArgs &a)
 {
     if (!cp_shape(a.N, a.K)) return false;
-    // bf16 and fp32 run the same kernel on a shape, so bf16 storage only
-    // rounds the fp32 results
+    // bf16 and fp32 run the same kernel on a shape (fp32 arrays that bf16
+    // could share are aligned), so bf16 storage only rounds the fp32 results
     if (a.bf16 && (a.D % 8 != 0 || a.proj.on)) return false;
     return vec_ok(a.D, a.x, a.dt, a.dy);
 }

@@ -95,10 +95,12 @@ struct SegPlan {
     int cps;    // checkpoint chunks per segment
 };
 
-// Stride 8 at 8 < N <= 16 on the channel-pair backward instead of the
-// 8-state one.
+// Stride 8 at 8 < N <= 16 on the channel-pair backward (1) or on the
+// 8-state one (0). The channel-pair kernel measured 5-6 % faster at configs
+// 1, 3a and 4 and 9-17 % on config 4's 2- and 4-way d_inner shards (6 %
+// slower on its 8-way shard).
 #ifndef MMS_BWD_CP_K8
-#define MMS_BWD_CP_K8 0
+#define MMS_BWD_CP_K8 1
 #endif
 // The channel-pair backward with 2 states per thread (256-thread CTAs) up to
 // this N (at most 32), else 4 states per thread (128-thread CTAs).
@@ -107,10 +109,13 @@ struct SegPlan {
 #endif
 
 // The shapes of the 8-state backward (mms_bwd_w8.cu): 8 < N <= 16, K == 8.
-inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8 && !MMS_BWD_CP_K8; }
+// With MMS_BWD_CP_K8 it runs them only where the channel-pair kernel cannot
+// (channel arrays not 16-byte aligned).
+inline bool w8_shape(int N, int K) { return groups_for(N) == 4 && N > 8 && K == 8; }
+inline bool w8_first(int N, int K) { return w8_shape(N, K) && !MMS_BWD_CP_K8; }
 // The shapes of the channel-pair backward (mms_bwd_cp.cu): 8 < N <= 64,
-// K a multiple of 8 up to 64, except the 8-state kernel's.
-inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64 && !w8_shape(N, K); }
+// K a multiple of 8 up to 64, except those the 8-state kernel takes first.
+inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64 && !w8_first(N, K); }
 inline bool cp_two_states(int N) { return N <= MMS_BWD_CP2_MAXN && N <= 32; }
 
 // Bounded waits of the TMA-staged kernels: polls of one stage's completion
@@ -130,9 +135,12 @@ inline SegPlan seg_plan(int Bt, int T, int D, int N, int K, bool backward)
     const int nchunk = (T + K - 1) / K;
     SegPlan p{1, nchunk};
     // Segments for one whole wave of the backward: the 8-state kernel runs 4
-    // CTAs per SM, the channel-pair and 4-state kernels (and the G-lane
-    // forward) 2. More segments than one wave holds only add local-pass work.
-    const long long per_sm = w8_shape(N, K) ? 4 : 2;
+    // CTAs per SM, the channel-pair and 4-state kernels 2. More segments than
+    // one wave holds only add local-pass work. The forward at stride 8 and
+    // 8 < N <= 16 plans for 4 per SM whichever backward runs (measured at
+    // config 3a: 378 us against 469 us with the 2-per-SM plan).
+    const bool s8 = groups_for(N) == 4 && N > 8 && K == 8;
+    const long long per_sm = backward ? (w8_first(N, K) ? 4 : 2) : (s8 ? 4 : 2);
     // Splitting costs a local pass over S-1 segments (about 40 % more work for
     // a fwd+bwd step), which pays only when the batch rows x channel blocks
     // leave SMs idle: below one CTA per SM, and for the 8-state backward (4

@@ -32,10 +32,10 @@ def test_step_bytes_match_the_roofline_units(bench):
 
 
 @pytest.mark.parametrize("shape,launches", [
-    ((16, 512, 2304, 16, 8), 3),     # config 1: whole-state forward, 8-state backward, reduction
+    ((16, 512, 2304, 16, 8), 3),     # config 1: whole-state forward, channel-pair backward, reduction
     ((1, 16384, 2048, 16, 8), 7),    # config 3a: both directions cut into time segments
-    ((4, 4096, 4096, 16, 8), 5),     # config 4 on two GPUs: G-lane forward unsegmented, backward in 2 segments
-    ((1, 16384, 2048, 64, 8), 7),    # config 3b: 4-state kernels, segmented
+    ((4, 4096, 4096, 16, 8), 3),     # config 4 on two GPUs: G-lane forward and backward unsegmented
+    ((1, 16384, 2048, 64, 8), 7),    # config 3b: G-lane forward, channel-pair backward, segmented
     ((4, 4096, 8192, 16, 8), 3),     # config 4 on one GPU
 ])
 def test_launch_count_follows_the_dispatch_rules(bench, shape, launches):
@@ -44,7 +44,8 @@ def test_launch_count_follows_the_dispatch_rules(bench, shape, launches):
 
 # (N, K, D)
 @pytest.mark.parametrize("shape,kernel", [
-    ((16, 8, 2304), "bwd_kernel_w8"),       # config 1
+    ((16, 8, 2304), "bwd_kernel_cp"),       # config 1
+    ((16, 8, 2302), "bwd_kernel_w8"),       # config 1's stride with unaligned channel arrays
     ((64, 8, 2048), "bwd_kernel_cp"),       # config 3b
     ((16, 64, 2304), "bwd_kernel_cp"),      # config 1 at the reference's stride
     ((8, 8, 2304), "bwd_kernel_k8"),        # d_state 8

@@ -43,9 +43,9 @@ def _with_withheld_item(fn, skip_item):
     return status, elapsed
 
 
-# (B, T, D, N, K, withheld item): the 8-state backward at stride 8 and the
-# channel-pair backward at stride 16, one CTA each (64 channels of one row),
-# and the channel-pair backward at d_state 32 (two CTAs of 32 channels)
+# (B, T, D, N, K, withheld item): the channel-pair backward at strides 8
+# and 16, one CTA each (64 channels of one row), and at d_state 32 (two CTAs
+# of 32 channels)
 BWD_CASES = [(1, 64, 64, 16, 8, 3), (1, 64, 64, 16, 16, 2), (1, 64, 64, 32, 8, 4)]
 
 

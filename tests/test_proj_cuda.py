@@ -7,8 +7,9 @@ kernels. Arbiter: the float64 oracle on the float64 prologue, with the chain
 rule applied in float64 for the logit and A gradients. Same normalised
 tolerances as the scan: 1e-5 forward, 1e-4 gradients. The shapes cover every
 kernel path the prologue runs through: the whole-state and G-lane forwards,
-time segments (local pass + combine), the TMA-staged and cp.async 8-state
-backwards and the 4-state backwards at other d_state and strides.
+time segments (local pass + combine), the channel-pair backward (4, 8 and
+16 lanes per pair), the cp.async 8-state backward (unaligned arrays at
+stride 8) and the 4-state backwards at other d_state and strides.
 """
 from __future__ import annotations
 
@@ -28,9 +29,9 @@ DT_MIN, DT_MAX = 0.001, 0.1
 DEV = "cuda"
 
 CASES = [
-    (16, 64, 2304, 16, 8),     # whole-state forward, TMA 8-state backward
-    (2, 100, 40, 16, 8),       # G-lane forward + time segments, TMA backward
-    (2, 130, 33, 16, 8),       # D % 4 != 0: cp.async paths
+    (16, 64, 2304, 16, 8),     # whole-state forward, channel-pair backward
+    (2, 100, 40, 16, 8),       # G-lane forward + time segments, channel-pair backward
+    (2, 130, 33, 16, 8),       # D % 4 != 0: cp.async paths (8-state backward)
     (3, 64, 20, 12, 8),        # d_state 12
     (2, 77, 21, 32, 64),       # d_state 32, stride 64 (4-state backward, recompute)
     (2, 100, 64, 32, 8),       # d_state 32: channel-pair backward, 8 lanes per pair

@@ -60,7 +60,7 @@ def _noalloc(lib, shape, seed):
 
 
 # (B, T, D, N, K) filling 97-100 % of the scratch; the stride picks the kernel:
-# 8-state (K = 8), channel-pair (K = 64), general with segment-start states (K = 200)
+# channel-pair (K = 8 and 64), general with segment-start states (K = 200)
 SHAPES = [(12, 300, 2048, 16, 8), (15, 512, 1024, 16, 64), (12, 512, 1024, 16, 200)]
 # a different shape run first, so the array holds another call's data
 OTHER = {8: (3, 100, 512, 16, 8), 64: (2, 200, 768, 16, 64), 200: (3, 333, 256, 16, 200)}
