@@ -136,8 +136,11 @@ __device__ __forceinline__ float2 shfl2(float2 v, int m) {
 }
 
 __device__ __forceinline__ float2 ld_pair(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+// bf16 to fp32 is exact: the bf16 bits are the top half of the fp32 word
+// (integer shift and mask, no conversion instruction).
 __device__ __forceinline__ float2 ld_pair(const __nv_bfloat16 *p) {
-    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(p));
+    const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+    return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
 }
 
 // Per-thread constants. Every float2 of a thread pairs its two channels

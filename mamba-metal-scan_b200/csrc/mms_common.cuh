@@ -69,7 +69,10 @@ __device__ __forceinline__ float softplus(float a) {
 // Storage element of the (B, T, D) channel arrays: float, or bf16 for the
 // bf16 entry points (the arithmetic is fp32 either way).
 __device__ __forceinline__ float to_f(float v) { return v; }
-__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+// bf16 to fp32 is exact: the bf16 bits become the top half of the fp32 word.
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) {
+    return __uint_as_float((uint32_t)__bfloat16_as_ushort(v) << 16);
+}
 template <typename E>
 __device__ __forceinline__ E from_f(float v) {
     if constexpr (sizeof(E) == 4) return v;
