@@ -205,7 +205,18 @@ fwd_kernel(const E *__restrict__ x, const E *__restrict__ dt,
 #ifndef MMS_FWD_ACC
 #define MMS_FWD_ACC 4
 #endif
-constexpr int S16_DPB = 128;                                 // channels (= threads) per CTA
+constexpr int S16_DPB = 128;                                 // channels per CTA
+// Lanes per channel: 1 (a thread holds all 16 states) or 2 (8 states each:
+// twice the warps per SM for the same shared memory; the two halves of y
+// meet by one shuffle). Two measured slower: config 1 118.6 against
+// 111.6 us, config 4 897 against 834 us.
+#ifndef MMS_S16_LPC
+#define MMS_S16_LPC 1
+#endif
+constexpr int S16_LPC = MMS_S16_LPC;
+static_assert(S16_LPC == 1 || S16_LPC == 2, "1 or 2 lanes per channel");
+constexpr int S16_THREADS = S16_DPB * S16_LPC;
+constexpr int S16_NP = 8 / S16_LPC;                          // state pairs per thread
 #ifndef MMS_S16_TT
 #define MMS_S16_TT 16
 #endif
@@ -225,17 +236,19 @@ constexpr int S16_UNROLL = MMS_S16_UNROLL;                   // steps unrolled i
 #ifndef MMS_FWD_POLY_PAIRS
 #define MMS_FWD_POLY_PAIRS 1
 #endif
-// `pair` is a constant after the step loop's unrolling, so each pair is
-// compiled to one of the two paths.
-__device__ __forceinline__ float2 fwd_decay(int pair, float2 x) {
-    return pair < MMS_FWD_POLY_PAIRS ? ex2_poly2(x) : ex2x2(x);
-}
-
-// The 16 decays 2^(dt * nan2) of one step.
-__device__ __forceinline__ void fwd_decays(float2 (&dA)[8], float dtv, const float2 (&nan2)[8]) {
+// The thread's decays 2^(dt * nan2) of step j. One lane per channel: its
+// pairs 0 .. MMS_FWD_POLY_PAIRS-1 take the polynomial; two lanes: those
+// pairs of each lane on even steps, the same share of the channel's
+// exponentials. `p` and `j & 1` are constants after the step loop's
+// unrolling, so each pair is compiled to one of the two paths.
+__device__ __forceinline__ void fwd_decays(float2 (&dA)[S16_NP], float dtv, const float2 (&nan2)[S16_NP],
+                                           int j) {
     const float2 dt2 = f2(dtv, dtv);
 #pragma unroll
-    for (int p = 0; p < 8; ++p) dA[p] = fwd_decay(p, mul2(dt2, nan2[p]));
+    for (int p = 0; p < S16_NP; ++p) {
+        const bool poly = p < MMS_FWD_POLY_PAIRS && (S16_LPC == 1 || (j & 1) == 0);
+        dA[p] = poly ? ex2_poly2(mul2(dt2, nan2[p])) : ex2x2(mul2(dt2, nan2[p]));
+    }
 }
 constexpr int S16_TT = MMS_S16_TT;                           // steps per staged tile
 constexpr int S16_MIN_CHANNELS = 148 * S16_DPB;
@@ -288,7 +301,7 @@ __device__ __forceinline__ bool fwd_wait(uint32_t bar, uint32_t parity, uint32_t
 // like the cp.async path's zero fill.
 // E: storage type of x, dt and y (float, or bf16 with TMA staging only).
 template <bool VEC, bool BULK, bool TMA, bool PROJ, bool SEG, typename E>
-__global__ void __launch_bounds__(S16_DPB, MMS_S16_MINB)
+__global__ void __launch_bounds__(S16_THREADS, MMS_S16_MINB)
 fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
                const float *__restrict__ aneg, const float *__restrict__ Bm,
                const float *__restrict__ Cm, E *__restrict__ y,
@@ -322,8 +335,11 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     const uint32_t bars = smem_u32(cks + S16Shape::CKF);   // TMA: FWD_STAGES barriers
 
     const int tid = threadIdx.x;
+    const int c = tid / S16_LPC, hf = tid % S16_LPC;       // channel in the CTA, its half
+    constexpr int NQ = S16_NP / 2;                         // state quads per thread
+    const int q0 = hf * NQ;                                // the thread's first quad
     const int d0 = blockIdx.x * DPB;
-    const int d = d0 + tid;
+    const int d = d0 + c;
     const int b = blockIdx.y;
     const bool dval = d < D;
     const int dcnt = min(DPB, D - d0);
@@ -336,13 +352,14 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     // the combine left the checkpoint at this segment's end; it is not rewritten
     const int ck_keep = SEG && sg + 1 < nsg ? (sg + 1) * cps - 1 : -1;
 
-    // -Aneg * log2(e) for the 16 states (zero past N): dA = 2^(dt * nan2).
-    float2 nan2[8], h[8];
+    // -Aneg * log2(e) for the thread's states (zero past N): dA = 2^(dt * nan2).
+    float2 nan2[S16_NP], h[S16_NP];
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
+    for (int p = 0; p < S16_NP; ++p) {
         float a0 = 0.f, a1 = 0.f;
-        if (dval && 2 * p < N) {
-            float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + 2 * p);
+        const int s = 4 * q0 + 2 * p;                      // the pair's first state
+        if (dval && s < N) {
+            float2 v = *reinterpret_cast<const float2 *>(aneg + (size_t)d * N + s);
             if (pj.on) v = f2(softplus(v.x), softplus(v.y));
             a0 = -v.x * MMS_LOG2E;
             a1 = -v.y * MMS_LOG2E;
@@ -358,9 +375,9 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
     if (SEG && sg > 0 && dval) {                           // state entering the segment
         const float *src = ckb + (size_t)(sg * cps - 1) * D * N;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (4 * q < N) {
-                const float4 w = *reinterpret_cast<const float4 *>(src + 4 * q);
+        for (int q = 0; q < NQ; ++q)
+            if (4 * (q0 + q) < N) {
+                const float4 w = *reinterpret_cast<const float4 *>(src + 4 * (q0 + q));
                 h[2 * q] = lo(w);
                 h[2 * q + 1] = hi(w);
             }
@@ -403,7 +420,7 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
                 tma3(dst + 4 * COFF, &maps.C, 0, tb + kt * TT, b, bar);
             }
         } else {
-            stage_tile<2, 2, DPB, 16, TT, DPB, VEC>(tile, xb, dtb, dtb, Bb, Cb, tb + kt * TT,
+            stage_tile<2, 2, DPB, 16, TT, S16_THREADS, VEC>(tile, xb, dtb, dtb, Bb, Cb, tb + kt * TT,
                                                     min(TT, te - tb - kt * TT), d0, D, N, tid);
         }
     };
@@ -465,19 +482,19 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
         const float *tile = tiles + (k % FWD_STAGES) * TT * ROWF;
         const E *tx = reinterpret_cast<const E *>(tile + XOFF);
         const E *tdt = reinterpret_cast<const E *>(tile + DOFF);
-        E *yrow = yse + (k & 1) * TT * DPB + tid;
+        E *yrow = yse + (k & 1) * TT * DPB + c;
         const int t0 = tb + k * TT;
         nck = 0;
 #pragma unroll S16_UNROLL
         for (int j = 0; j < TT; ++j) {
             // Steps past T were staged as zeros: dt = 0 gives dA = 1, b = 0.
-            const float xv = to_f(tx[j * XROW + tid]);
-            float dtv = to_f(tdt[j * XROW + tid]);
+            const float xv = to_f(tx[j * XROW + c]);
+            float dtv = to_f(tdt[j * XROW + c]);
             if (pj.on) dtv = fmaf(pj.range, sigmoid_fast(dtv), pj.lo);
-            float2 dAc[8];
-            fwd_decays(dAc, dtv, nan2);
-            const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW);
-            const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW);
+            float2 dAc[S16_NP];
+            fwd_decays(dAc, dtv, nan2, j);
+            const float4 *bp = reinterpret_cast<const float4 *>(tile + BOFF + j * BROW) + q0;
+            const float4 *cp = reinterpret_cast<const float4 *>(tile + COFF + j * BROW) + q0;
             const float bx = dtv * xv;
             const float2 bx2 = f2(bx, bx);
             // y = sum_n C*h over MMS_FWD_ACC independent partial sums (shorter chains)
@@ -485,7 +502,7 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
 #pragma unroll
             for (int q = 0; q < MMS_FWD_ACC; ++q) acc[q] = f2(0.f, 0.f);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int q = 0; q < NQ; ++q) {
                 const float4 Bv = bp[q], Cv = cp[q];
                 h[2 * q] = fma2(dAc[2 * q], h[2 * q], mul2(bx2, lo(Bv)));
                 h[2 * q + 1] = fma2(dAc[2 * q + 1], h[2 * q + 1], mul2(bx2, hi(Bv)));
@@ -494,29 +511,34 @@ fwd_kernel_s16(const E *__restrict__ x, const E *__restrict__ dt,
             }
 #pragma unroll
             for (int q = 1; q < MMS_FWD_ACC; ++q) acc[0] = add2(acc[0], acc[q]);
+            float yv = acc[0].x + acc[0].y;
+            if constexpr (S16_LPC == 2) yv += __shfl_xor_sync(0xffffffffu, yv, 1);
             const int t = t0 + j;
-            if constexpr (BULK) yrow[j * DPB] = from_f<E>(acc[0].x + acc[0].y);
-            else if (dval && t < te) yb[(size_t)t * D] = from_f<E>(acc[0].x + acc[0].y);
+            if constexpr (BULK) {
+                if (hf == 0) yrow[j * DPB] = from_f<E>(yv);
+            } else if (hf == 0 && dval && t < te) {
+                yb[(size_t)t * D] = from_f<E>(yv);
+            }
             if (t == next_ck && (!SEG || t < te)) {        // uniform across the CTA
                 float *o = ckb + (size_t)chunk * D * N;
                 const bool keep = SEG && chunk == ck_keep;
                 int swz = 0;                               // quad index XOR (TMA slabs)
                 if (BULK && nck < 2 && !keep) {
                     if constexpr (TMA) {
-                        o = cks + ((k & 1) * 2 + nck) * DPB * CKROW + tid * CKROW;
-                        swz = (tid >> 1) & 3;
+                        o = cks + ((k & 1) * 2 + nck) * DPB * CKROW + c * CKROW;
+                        swz = (c >> 1) & 3;
                     } else {
-                        o = cks + ((k & 1) * 2 + nck) * DPB * N + tid * N;
+                        o = cks + ((k & 1) * 2 + nck) * DPB * N + c * N;
                     }
                     if (nck == 0) ck0 = chunk; else ck1 = chunk;
                     ++nck;
                 }
                 if (dval && !keep) {
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
-                        if (4 * q < N)
-                            st4(o + 4 * (q ^ swz), make_float4(h[2 * q].x, h[2 * q].y,
-                                                               h[2 * q + 1].x, h[2 * q + 1].y));
+                    for (int q = 0; q < NQ; ++q)
+                        if (4 * (q0 + q) < N)
+                            st4(o + 4 * ((q0 + q) ^ swz), make_float4(h[2 * q].x, h[2 * q].y,
+                                                                      h[2 * q + 1].x, h[2 * q + 1].y));
                 }
                 ++chunk;
                 next_ck = min(next_ck + K, T - 1);
@@ -564,7 +586,7 @@ static cudaError_t launch_fwd_s16_q(const FwdArgs &a, const FwdMaps &maps, SegPl
     cudaError_t e = smem_opt_in<fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E>>(smem);
     if (e != cudaSuccess) return e;
     dim3 grid((a.D + S16Shape::DPB - 1) / S16Shape::DPB, a.Bt, sp.S);
-    fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E><<<grid, S16_DPB, smem, stream>>>(
+    fwd_kernel_s16<VEC, BULK, TMA, PROJ, SEG, E><<<grid, S16_THREADS, smem, stream>>>(
         reinterpret_cast<const E *>(a.x), reinterpret_cast<const E *>(a.dt), a.aneg, a.B, a.C,
         reinterpret_cast<E *>(a.y), a.ckpt, a.T, a.D, a.N, a.K, sp.cps * a.K, sp.cps, maps,
         a.proj, tma_wait_limit(), tma_skip_item());
