@@ -868,8 +868,8 @@ cudaError_t launch_bwd(const BwdArgs &a, cudaStream_t stream)
 {
     const BwdWorkspace w = bwd_workspace_layout(a.Bt, a.T, a.D, a.N, a.K);
     if (a.bf16) {
-        // bf16 channel arrays: the stride-8 backwards (8-state for 8 < N <= 16,
-        // else 4-state), 16-byte staging
+        // bf16 channel arrays: the stride-8 backwards (channel-pair for
+        // 8 < N <= 64, else 4-state), 16-byte aligned arrays
         if (a.K != GRP || a.D % 8 != 0 || a.proj.on || !vec_ok(a.D, a.x, a.dt, a.dy) ||
             !vec_ok(a.D, a.dx, a.ddt))
             return cudaErrorInvalidValue;

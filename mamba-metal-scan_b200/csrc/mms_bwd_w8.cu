@@ -1,5 +1,10 @@
 // Backward selective scan, 8 states per lane (8 < N <= 16, checkpoint stride 8).
 //
+// The channel-pair kernel (mms_bwd_cp.cu) runs these shapes when the channel
+// arrays are 16-byte aligned (it measured 5-6 % faster); this one runs them
+// otherwise, on cp.async staging, and for every such shape in a build with
+// MMS_BWD_CP_K8=0, where its TMA staging is used.
+//
 // Same mathematics as mms_bwd.cu (reference mamba_metal/scan.py:26-34, kernel
 // ssm_bwd at :132-261); a different decomposition for the d_state 12/16 case:
 // two lanes share a channel and each holds 8 of its 16 states. Compared with

@@ -196,8 +196,9 @@ struct SegLocalArgs {
 };
 cudaError_t launch_seg_local(const SegLocalArgs &a, bool backward, cudaStream_t stream);
 
-// Backward with 8 states per lane (mms_bwd_w8.cu) for 8 < N <= 16 and K == 8;
-// same workspace regions as the general backward.
+// Backward with 8 states per lane (mms_bwd_w8.cu) for 8 < N <= 16 and K == 8
+// where the channel-pair backward does not run (see w8_first); same
+// workspace regions as the general backward.
 bool bwd_w8_applies(int N, int K);
 cudaError_t launch_bwd_w8(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
                           int nblk, SegPlan sp, cudaStream_t stream);
