@@ -123,10 +123,12 @@ def test_long_sequences_match_the_float64_oracle(bt, t_len, d, n, chunk, slow):
     assert max_rel(ckpt, ckpt64) <= FWD_TOL
 
 
-# The channel-pair backward at d_state 20..64 (8 or 16 lanes per channel
-# pair): every stride class, a channel count that leaves a CTA partly empty,
-# and a long sequence that also runs time segments.
-PAIRS = [(2, 200, 64, 32, 8, False), (1, 333, 48, 20, 16, False), (2, 150, 40, 48, 24, False),
+# The channel-pair backward at d_state 12 (4 lanes per pair, states 12..15
+# padded) and 20..64 (8 or 16 lanes per channel pair): every stride class, a
+# channel count that leaves a CTA partly empty, and long sequences that also
+# run time segments.
+PAIRS = [(2, 200, 64, 12, 8, False), (1, 1500, 32, 12, 24, True),
+         (2, 200, 64, 32, 8, False), (1, 333, 48, 20, 16, False), (2, 150, 40, 48, 24, False),
          (1, 257, 32, 64, 64, False), (1, 100, 36, 64, 8, False), (2, 130, 24, 28, 40, False),
          (1, 3000, 96, 32, 16, True), (1, 2500, 32, 64, 8, True)]
 
