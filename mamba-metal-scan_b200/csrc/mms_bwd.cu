@@ -814,8 +814,9 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
             return e;
     }
     dim3 grid(w.nblk, a.Bt, sp.S);
+    int nblk = w.nblk;                                 // CTAs along D that wrote dB|dC partials
     if (G >= 4 && MMS_BWD_CP && bwd_cp_applies(a)) {
-        e = launch_bwd_cp(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
+        e = launch_bwd_cp(a, part_bc, part_a, seg_e, sp, stream, &nblk);
     } else if (G == 4 && bwd_w8_applies(a.N, a.K) && (MMS_BWD_W8 || a.bf16)) {
         e = launch_bwd_w8(a, part_bc, part_a, seg_e, w.nblk, sp, stream);
     } else if (a.K == GRP) {
@@ -844,7 +845,7 @@ static cudaError_t launch_bwd_gvp(const BwdArgs &a, const BwdWorkspace &w, cudaS
     const int nb_bc = blocks((size_t)a.Bt * a.T * 2 * a.N / 4);
     const size_t dn = (size_t)a.D * a.N;
     const int nb_a = blocks(dn / 4);
-    reduce_kernel<<<nb_bc + nb_a, 256, 0, stream>>>(part_bc, a.dB, a.dC, a.Bt, a.T, a.N, w.nblk,
+    reduce_kernel<<<nb_bc + nb_a, 256, 0, stream>>>(part_bc, a.dB, a.dC, a.Bt, a.T, a.N, nblk,
                                                     nb_bc, part_a, a.daneg, a.Bt * sp.S, dn,
                                                     a.aneg, a.proj.on);
     return cudaGetLastError();

@@ -85,12 +85,14 @@ constexpr float CP_LN2 = 0.6931471805599453f;
 // Geometry: NQ lanes share a channel pair, each lane holding SPT states of
 // both channels (SPT = 4: 128-thread CTAs; SPT = 2: 256-thread CTAs, half the
 // registers per thread). Both give 256 / groups_for(N) channels per CTA.
-template <int NQ_, int SPT_>
+template <int NQ_, int SPT_, int THREADS_ = 512 / SPT_>
 struct CpGeo {
     static constexpr int NQ = NQ_, SPT = SPT_;
     static_assert((SPT == 4 && (NQ == 4 || NQ == 8 || NQ == 16)) || (SPT == 2 && (NQ == 8 || NQ == 16)),
                   "4 states on 4, 8 or 16 lanes, or 2 states on 8 or 16 lanes");
-    static constexpr int THREADS = 512 / SPT;
+    static constexpr int THREADS = THREADS_;
+    static_assert(THREADS == 512 / SPT || (SPT == 4 && THREADS == 256), "128 or 256 threads at 4 states");
+    static constexpr int MINB = THREADS * SPT == 1024 ? 1 : 2;  // CTAs per SM the registers allow
     static constexpr int WARPS = THREADS / 32;
     static constexpr int LOGQ = NQ == 4 ? 2 : NQ == 8 ? 3 : 4;
     static constexpr int DPB = 2 * THREADS / NQ;            // channels per CTA
@@ -410,7 +412,7 @@ struct CpCursor {
 };
 
 template <typename E, typename G, bool PROJ, bool ONEBAR>
-__global__ void __launch_bounds__(G::THREADS, 2)
+__global__ void __launch_bounds__(G::THREADS, G::MINB)
 bwd_kernel_cp(const float *__restrict__ aneg, E *__restrict__ dx, E *__restrict__ ddt,
               float *__restrict__ part_bc, float *__restrict__ part_a,
               const float *__restrict__ seg_e, int T, int D, int N, int M, int nblk, int cps,
@@ -626,13 +628,14 @@ bool build_cp_maps(const BwdArgs &a, CpMaps *m)
            tma_encode(fn, &m->C, a.C, 3, dB, bB) && tma_encode(fn, &m->ck, a.ckpt, 4, dK, bK);
 }
 
-// One barrier per item where the double buffers still leave 2 CTAs per SM
-// (228 KB of shared memory, 1 KB of it reserved per CTA), except at 8 lanes
-// per pair (d_state 20..32), which measured 1.5 % slower with it.
+// One barrier per item where the double buffers still leave the CTAs per SM
+// that the registers allow (228 KB of shared memory, 1 KB of it reserved per
+// CTA), except at 8 lanes per pair (d_state 20..32), which measured 1.5 %
+// slower with it.
 template <typename E, typename G>
 bool cp_onebar(int M)
 {
-    return G::NQ != 8 && CpTile<E, G>::smem(M, 2) + 1024 <= 228 * 1024 / 2;
+    return G::NQ != 8 && CpTile<E, G>::smem(M, 2) + 1024 <= 228 * 1024 / G::MINB;
 }
 
 template <typename E, typename G, bool PROJ, bool ONEBAR>
@@ -646,7 +649,7 @@ cudaError_t launch_cpb(const BwdArgs &a, float *part_bc, float *part_a, const fl
     if (e != cudaSuccess) return e;                        // one opt-in size for every M
     const uint32_t limit = tma_wait_limit();
     const int skip = tma_skip_item();
-    dim3 grid((a.D + G::DPB - 1) / G::DPB, a.Bt, sp.S);
+    dim3 grid(nblk, a.Bt, sp.S);                           // nblk = ceil(D / DPB)
     bwd_kernel_cp<E, G, PROJ, ONEBAR><<<grid, G::THREADS, Q::smem(M, bufs), stream>>>(
         a.aneg, reinterpret_cast<E *>(a.dx), reinterpret_cast<E *>(a.ddt), part_bc, part_a, seg_e,
         a.T, a.D, a.N, M, nblk, sp.cps, maps, a.proj, limit, skip);
@@ -685,12 +688,26 @@ bool bwd_cp_applies(const BwdArgs &a)
     return vec_ok(a.D, a.x, a.dt, a.dy);
 }
 
+int cp_channels_per_cta(int N)
+{
+    switch (groups_for(N)) {
+    case 4: return CpGeo<4, 4>::DPB;
+    case 8: return CpGeo<8, 4>::DPB;
+    case 16: return MMS_BWD_CP16_WIDE ? CpGeo<16, 4, 256>::DPB : CpGeo<16, 4>::DPB;
+    default: return 0;
+    }
+}
+
 cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
-                          int nblk, SegPlan sp, cudaStream_t stream)
+                          SegPlan sp, cudaStream_t stream, int *nblk_used)
 {
     const int G = groups_for(a.N);
+    const int dpb = cp_channels_per_cta(a.N);
+    if (dpb == 0) return cudaErrorInvalidValue;
+    const int nblk = (a.D + dpb - 1) / dpb;
+    *nblk_used = nblk;
 #if MMS_BWD_CP2_MAXN > 0
-    if (cp_two_states(a.N)) {
+    if (cp_two_states(a.N)) {                              // same channels per CTA as below
         switch (G) {
         case 4: return launch_cp_g<CpGeo<8, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
         case 8: return launch_cp_g<CpGeo<16, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
@@ -701,7 +718,10 @@ cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const
     switch (G) {
     case 4: return launch_cp_g<CpGeo<4, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
     case 8: return launch_cp_g<CpGeo<8, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    case 16: return launch_cp_g<CpGeo<16, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 16:
+        return MMS_BWD_CP16_WIDE
+                   ? launch_cp_g<CpGeo<16, 4, 256>>(a, part_bc, part_a, seg_e, nblk, sp, stream)
+                   : launch_cp_g<CpGeo<16, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -117,6 +117,12 @@ inline bool w8_first(int N, int K) { return w8_shape(N, K) && !MMS_BWD_CP_K8; }
 // K a multiple of 8 up to 64, except those the 8-state kernel takes first.
 inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64 && !w8_first(N, K); }
 inline bool cp_two_states(int N) { return N <= MMS_BWD_CP2_MAXN && N <= 32; }
+// At 32 < N <= 64 the channel-pair backward runs 256-thread CTAs of 32
+// channels (1 per SM) instead of 128-thread CTAs of 16 (2 per SM): the same
+// CTA slots, half the per-CTA dB|dC partials.
+#ifndef MMS_BWD_CP16_WIDE
+#define MMS_BWD_CP16_WIDE 1
+#endif
 
 // Bounded waits of the TMA-staged kernels: polls of one stage's completion
 // barrier before a kernel gives up (default 2^22), and a staged item whose
@@ -208,10 +214,14 @@ int w8_take_timeout();
 
 // Backward on channel pairs (mms_bwd_cp.cu) for cp_shape() with TMA-ready
 // arrays (D % 4 == 0 and 16-byte aligned; bf16: D % 8 == 0, no prologue);
-// same workspace regions as the general backward.
+// same workspace regions as the general backward. Its CTAs cover
+// cp_channels_per_cta(N) channels, at least the general kernel's 256 /
+// groups_for(N), so its per-CTA dB|dC partials fit the workspace;
+// *nblk_used receives how many CTAs along D wrote them.
 bool bwd_cp_applies(const BwdArgs &a);
+int cp_channels_per_cta(int N);
 cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
-                          int nblk, SegPlan sp, cudaStream_t stream);
+                          SegPlan sp, cudaStream_t stream, int *nblk_used);
 int cp_take_timeout();
 
 // Gate epilogue out = (y + D_skip) * silu(z) (mms_gate.cu); rows = Bt * T.
