@@ -27,15 +27,19 @@
 // reduction over those bits are select-free; B and C are rewritten once per
 // sub-chunk into the lane orders in shared memory. The lowest pair bit left,
 // if any, reduces by kind (dB on one lane, dC on its partner).
-//   SPT = 4 (the default; 128-thread CTAs, about 250 registers, 2 CTAs per SM)
-//     on NQ = 4, 8, 16 lanes for N <= 16, 32, 64;
+//   SPT = 4 (the default; about 250 registers) on NQ = 4, 8, 16 lanes for
+//     N <= 16, 32, 64, in 128-thread CTAs (2 per SM), at N > 32 in 256-thread
+//     CTAs (1 per SM, MMS_BWD_CP16_WIDE): the same CTA slots, with 32 instead
+//     of 16 channels per CTA, which halves the per-CTA dB|dC partials
+//     (config 3b backward 3290 -> 3174 us);
 //   SPT = 2 (256-thread CTAs at 128 registers, 2 per SM: twice the warps) on
 //     NQ = 8, 16 lanes for N <= 16, 32, built when MMS_BWD_CP2_MAXN is set.
 //     It measures slower (config 1 at K = 8: 443 against 346 us, N = 32:
 //     897 against 670 us): per state-step it loads, shuffles and selects
 //     more than the extra warps hide.
-// Both give 256 / groups_for(N) channels per CTA, the general backward's
-// block, so they share its workspace.
+// The 128-thread CTAs cover 256 / groups_for(N) channels, the general
+// backward's block, the 256-thread ones twice that; either fits its
+// workspace.
 //
 // Time: a CTA walks its checkpoint chunks last to first in 8-step
 // sub-chunks. A sub-chunk is rebuilt from the state entering it (all 8
@@ -83,8 +87,7 @@ constexpr int CP_MAXM = 8;                    // sub-chunks per chunk (K <= 64)
 constexpr float CP_LN2 = 0.6931471805599453f;
 
 // Geometry: NQ lanes share a channel pair, each lane holding SPT states of
-// both channels (SPT = 4: 128-thread CTAs; SPT = 2: 256-thread CTAs, half the
-// registers per thread). Both give 256 / groups_for(N) channels per CTA.
+// both channels, in CTAs of THREADS threads: 2 * THREADS / NQ channels.
 template <int NQ_, int SPT_, int THREADS_ = 512 / SPT_>
 struct CpGeo {
     static constexpr int NQ = NQ_, SPT = SPT_;
