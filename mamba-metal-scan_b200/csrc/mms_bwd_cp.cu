@@ -29,7 +29,7 @@
 // if any, reduces by kind (dB on one lane, dC on its partner).
 //   SPT = 4 (the default; about 250 registers) on NQ = 4, 8, 16 lanes for
 //     N <= 16, 32, 64, in 128-thread CTAs (2 per SM), at N > 32 in 256-thread
-//     CTAs (1 per SM, MMS_BWD_CP16_WIDE): the same CTA slots, with 32 instead
+//     CTAs (1 per SM, MMS_BWD_CP_WIDE): the same CTA slots, with 32 instead
 //     of 16 channels per CTA, which halves the per-CTA dB|dC partials
 //     (config 3b backward 3290 -> 3174 us);
 //   SPT = 2 (256-thread CTAs at 128 registers, 2 per SM: twice the warps) on
@@ -693,12 +693,9 @@ bool bwd_cp_applies(const BwdArgs &a)
 
 int cp_channels_per_cta(int N)
 {
-    switch (groups_for(N)) {
-    case 4: return CpGeo<4, 4>::DPB;
-    case 8: return CpGeo<8, 4>::DPB;
-    case 16: return MMS_BWD_CP16_WIDE ? CpGeo<16, 4, 256>::DPB : CpGeo<16, 4>::DPB;
-    default: return 0;
-    }
+    const int G = groups_for(N);
+    if (G != 4 && G != 8 && G != 16) return 0;
+    return (MMS_BWD_CP_WIDE & G ? 512 : 256) / G;
 }
 
 cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const float *seg_e,
@@ -710,7 +707,7 @@ cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const
     const int nblk = (a.D + dpb - 1) / dpb;
     *nblk_used = nblk;
 #if MMS_BWD_CP2_MAXN > 0
-    if (cp_two_states(a.N)) {                              // same channels per CTA as below
+    if (cp_two_states(a.N) && !(MMS_BWD_CP_WIDE & G)) {    // same channels per CTA as 128-thread 4-state
         switch (G) {
         case 4: return launch_cp_g<CpGeo<8, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
         case 8: return launch_cp_g<CpGeo<16, 2>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
@@ -718,13 +715,12 @@ cudaError_t launch_bwd_cp(const BwdArgs &a, float *part_bc, float *part_a, const
         }
     }
 #endif
+    constexpr int T4 = MMS_BWD_CP_WIDE & 4 ? 256 : 128, T8 = MMS_BWD_CP_WIDE & 8 ? 256 : 128,
+                  T16 = MMS_BWD_CP_WIDE & 16 ? 256 : 128;
     switch (G) {
-    case 4: return launch_cp_g<CpGeo<4, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    case 8: return launch_cp_g<CpGeo<8, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
-    case 16:
-        return MMS_BWD_CP16_WIDE
-                   ? launch_cp_g<CpGeo<16, 4, 256>>(a, part_bc, part_a, seg_e, nblk, sp, stream)
-                   : launch_cp_g<CpGeo<16, 4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 4: return launch_cp_g<CpGeo<4, 4, T4>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 8: return launch_cp_g<CpGeo<8, 4, T8>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
+    case 16: return launch_cp_g<CpGeo<16, 4, T16>>(a, part_bc, part_a, seg_e, nblk, sp, stream);
     default: return cudaErrorInvalidValue;
     }
 }

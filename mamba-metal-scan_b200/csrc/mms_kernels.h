@@ -117,11 +117,12 @@ inline bool w8_first(int N, int K) { return w8_shape(N, K) && !MMS_BWD_CP_K8; }
 // K a multiple of 8 up to 64, except those the 8-state kernel takes first.
 inline bool cp_shape(int N, int K) { return N > 8 && N <= 64 && K % 8 == 0 && K <= 64 && !w8_first(N, K); }
 inline bool cp_two_states(int N) { return N <= MMS_BWD_CP2_MAXN && N <= 32; }
-// At 32 < N <= 64 the channel-pair backward runs 256-thread CTAs of 32
-// channels (1 per SM) instead of 128-thread CTAs of 16 (2 per SM): the same
-// CTA slots, half the per-CTA dB|dC partials.
-#ifndef MMS_BWD_CP16_WIDE
-#define MMS_BWD_CP16_WIDE 1
+// The lane widths (groups_for(N): bit 4, 8, 16) at which the channel-pair
+// backward runs 256-thread CTAs (1 per SM) instead of 128-thread CTAs (2 per
+// SM): the same CTA slots, twice the channels per CTA, half the per-CTA
+// dB|dC partials. Default: 16 (32 < N <= 64).
+#ifndef MMS_BWD_CP_WIDE
+#define MMS_BWD_CP_WIDE 16
 #endif
 
 // Bounded waits of the TMA-staged kernels: polls of one stage's completion
